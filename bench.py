@@ -1,0 +1,496 @@
+#!/usr/bin/env python
+"""bench.py - cdclq-b200 benchmark under the driver's contract.
+
+Workload: a TinyLlama-1.1B-shaped model, 22 decoder layers x 7 linear layers
+(q 2048x2048, k/v 256x2048, o 2048x2048, gate/up 5632x2048, down 2048x5632) = 9.69e8 weights, random-init
+bf16 weights ~ N(0, 0.02^2) (widened to f32 as the reference does for bf16 checkpoints, src/io.rs:37-44),
+and per distinct layer input (q/k/v, o, gate/up, down: 88 Hessians) a synthetic Hessian H = X^T X from
+128 x 2048 = 262144 seeded tokens distributed as configs[0] (per-channel log-normal scale sigma = 1,
+0.5 % channels x20, 1 % dead channels).  Settings: 3-bit, group 128, --mse-grid, reference defaults otherwise
+(block 128, sub-block 64, damp 0.01, act-order, CDCL, 10 passes, tol 1e-3), row chunk pinned to 128 rows.
+
+One step = quantizing the whole model from resident inputs: 88 factorisations (the q/k/v and gate/up layers
+share theirs), the GPTQ pass and the CDCL repair of all 154 layers.  The Hessians are inputs, as they are for
+the reference's `cdclq quantize` (captured by a separate script).
+
+Legs:
+  value     device-resident inputs (W, H in HBM; 7.7 GB, larger than L2), CUDA events on the stream
+  e2e       the public C ABI with pinned HOST buffers (cdclq_quantize_batch, on_device = 0): H2D of W and H and
+            D2H of codes/scales/zeros inside the timed region
+  cpu_baseline  the CPU oracle (C++ restatement of the reference's rayon path) on a bounded sample, rank 0,
+            N = 1 only
+  --impl reference  the oracle port on the host cores (the Rust reference cannot be built here), same sample
+
+N > 1: one process per GPU (torchrun); every layer's rows are split across ranks in whole row chunks (rows are
+independent and row chunks are the reference's unit of conflict selection and stopping), so the result is
+identical to N = 1; the per-layer losses are all-reduced over NCCL.  Weak/strong: strong (the model is fixed).
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cdcl-gptq_b200"))
+
+METRIC = "seconds per model quantized (incl. CDCL repair) at 1/2/4/8 B200; weights/sec"
+HIDDEN, INTER, N_LAYERS, KV_OUT = 2048, 5632, 22, 256
+TOKENS = 128 * 2048
+ROW_CHUNK = 128
+
+# (name, d_out, d_in, input kind)
+BLOCK = [("q_proj", HIDDEN, HIDDEN, "attn"), ("k_proj", KV_OUT, HIDDEN, "attn"), ("v_proj", KV_OUT, HIDDEN, "attn"),
+         ("o_proj", HIDDEN, HIDDEN, "o"), ("gate_proj", INTER, HIDDEN, "mlp"), ("up_proj", INTER, HIDDEN, "mlp"),
+         ("down_proj", HIDDEN, INTER, "down")]
+INPUT_DIM = {"attn": HIDDEN, "o": HIDDEN, "mlp": HIDDEN, "down": INTER}
+
+
+def bench_config():
+    from cdclq.abi import Config
+
+    return Config(bits=3, group=128, mse_grid=True, row_chunk=ROW_CHUNK)
+
+
+# ------------------------------------------------------------------------------------------------------------
+# seeded synthetic inputs (torch is plumbing here: RNG and the TF32 GEMM that builds H from bf16 tokens)
+def channel_profile(n, seed, torch, device):
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    s = torch.exp(torch.randn(n, generator=g, dtype=torch.float64))
+    perm = torch.randperm(n, generator=g)
+    n_out = max(1, round(0.005 * n))
+    n_dead = max(1, round(0.01 * n))
+    s[perm[:n_out]] *= 20.0
+    s[perm[n_out:n_out + n_dead]] = 0.0
+    return s.to(device=device, dtype=torch.float32)
+
+
+def make_hessian(n, seed, tokens, torch, device):
+    """H = X^T X over `tokens` seeded tokens; X is bf16-representable so the TF32 GEMM products are exact."""
+    scale = channel_profile(n, seed, torch, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    h = torch.zeros(n, n, dtype=torch.float64, device=device)
+    chunk = 8192
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for t0 in range(0, tokens, chunk):
+            tc = min(chunk, tokens - t0)
+            x = (torch.randn(tc, n, generator=g, device=device) * scale).to(torch.bfloat16).float()
+            h += (x.t() @ x).double()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    return h.float().contiguous()
+
+
+def make_weight(d_out, n, seed, torch, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = (torch.randn(d_out, n, generator=g, device=device) * 0.02).to(torch.bfloat16).float()
+    return w.contiguous()
+
+
+def model_layers(n_layers=N_LAYERS):
+    """[(layer name, d_out, d_in, input index)], inputs [(name, n)]."""
+    layers, inputs = [], []
+    for b in range(n_layers):
+        idx = {}
+        for kind in ("attn", "o", "mlp", "down"):
+            idx[kind] = len(inputs)
+            inputs.append(("model.layers.%d.%s" % (b, kind), INPUT_DIM[kind]))
+        for name, d_out, d_in, kind in BLOCK:
+            layers.append(("model.layers.%d.%s" % (b, name), d_out, d_in, idx[kind]))
+    return layers, inputs
+
+
+def generate(torch, device, n_layers=N_LAYERS, tokens=TOKENS):
+    layers, inputs = model_layers(n_layers)
+    H = [make_hessian(n, 1000 + i, tokens, torch, device) for i, (_, n) in enumerate(inputs)]
+    W = [make_weight(d_out, d_in, 50000 + i, torch, device) for i, (_, d_out, d_in, _) in enumerate(layers)]
+    return layers, inputs, H, W
+
+
+# ------------------------------------------------------------------------------------------------------------
+def shard_rows(d_out, rank, world):
+    """Contiguous row range of this rank, in whole row chunks."""
+    chunks = (d_out + ROW_CHUNK - 1) // ROW_CHUNK
+    c0 = chunks * rank // world
+    c1 = chunks * (rank + 1) // world
+    return min(c0 * ROW_CHUNK, d_out), min(c1 * ROW_CHUNK, d_out)
+
+
+class Batch:
+    """Preallocated outputs + C descriptor tables for one cdclq_quantize_batch call."""
+
+    def __init__(self, torch, layers, inputs, H, W, cfg, rank, world, on_device):
+        from cdclq.abi import CBatchInput, CBatchLayer, CLayerStats, num_groups
+
+        self.cfg = cfg
+        self.on_device = on_device
+        self.keep = []
+        self.ins = (CBatchInput * len(inputs))()
+        for i, (_, n) in enumerate(inputs):
+            h = H[i]
+            self.keep.append(h)
+            self.ins[i].h = h.data_ptr()
+            self.ins[i].n = n
+        rows = []
+        for (name, d_out, d_in, inp), w in zip(layers, W):
+            r0, r1 = shard_rows(d_out, rank, world)
+            if r1 > r0:
+                rows.append((name, d_out, d_in, inp, w, r0, r1))
+        self.lys = (CBatchLayer * len(rows))()
+        self.stats = [CLayerStats() for _ in rows]
+        self.outs = []
+        self.h2d_bytes = sum(int(h.numel()) * 4 for h in H)
+        self.d2h_bytes = 0
+        dev = "cuda" if on_device else "cpu"
+        for i, (name, d_out, d_in, inp, w, r0, r1) in enumerate(rows):
+            ng = num_groups(cfg, d_in)
+            rs = r1 - r0
+            wv = w[r0:r1]
+            self.keep.append(wv)
+            o = dict(perm=np.zeros(d_in, np.uint32), gbits=np.zeros(ng, np.uint8),
+                     codes=torch.empty(rs, d_in, dtype=torch.uint8, device=dev, pin_memory=not on_device),
+                     scales=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device),
+                     zeros=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device))
+            self.outs.append(o)
+            L = self.lys[i]
+            L.w = wv.data_ptr()
+            L.d_out = rs
+            L.input = inp
+            L.perm = o["perm"].ctypes.data
+            L.gbits = o["gbits"].ctypes.data
+            L.codes = o["codes"].data_ptr()
+            L.scales = o["scales"].data_ptr()
+            L.zeros = o["zeros"].data_ptr()
+            L.stats = ctypes.pointer(self.stats[i])
+            self.h2d_bytes += rs * d_in * 4
+            self.d2h_bytes += rs * d_in + 2 * rs * ng * 4 + d_in * 4 + ng
+        self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1) in rows)
+
+    def run(self, stream_handle):
+        import cdclq
+
+        c = self.cfg.to_c()
+        cdclq._lib.check(cdclq.lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys),
+                                                          ctypes.byref(c), 1 if self.on_device else 0,
+                                                          ctypes.c_void_p(stream_handle)))
+
+
+# ------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = float(p[2])
+                power.append(float(p[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def fp32_simt_peak_tflops(torch):
+    """Measured FP32 CUDA-core peak: cuBLAS SGEMM with TF32 disabled (FFMA), best of 5."""
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n = 8192
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        for _ in range(2):
+            a @ b
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            a @ b
+            e1.record()
+            e1.synchronize()
+            best = max(best, 2.0 * n ** 3 / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        return best
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ------------------------------------------------------------------------------------------------------------
+def cpu_sample(layers, inputs, H, W, cfg):
+    """Time the CPU oracle on a bounded sample and extrapolate to the whole model (stated in `sample`).
+
+    Sample: the factorisation of one 2048-wide and one 5632-wide input, and one 128-row chunk of q_proj
+    (d_in 2048) and of down_proj (d_in 5632).  Model time = 22 x [sum over the block's 4 inputs of the
+    factorisation time of that width + sum over the block's 7 layers of (chunk time of that width) x (row
+    chunks of the layer) / cores], i.e. perfect scaling of row chunks over the host cores.
+    """
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    cores = orc.max_threads()
+    t_prep, t_chunk = {}, {}
+    by_width = {}
+    for (name, d_out, d_in, inp) in layers[:7]:
+        by_width.setdefault(d_in, (name, d_out, d_in, inp))
+    t0 = time.time()
+    for d_in, (name, d_out, _, inp) in by_width.items():
+        li = [l[0] for l in layers].index(name)
+        h = H[inp].cpu().numpy()
+        w = W[li][:ROW_CHUNK].cpu().numpy()
+        ql, st = orc.quantize_layer(w, w.shape[0], d_in, h, None, inputs[inp][0], cfg)
+        t_prep[d_in] = st.secs_prepare
+        t_chunk[d_in] = st.secs_quant
+    wall = time.time() - t0
+    per_block = 0.0
+    for kind, n in INPUT_DIM.items():
+        per_block += t_prep[n]
+    for name, d_out, d_in, kind in BLOCK:
+        chunks = (d_out + ROW_CHUNK - 1) // ROW_CHUNK
+        per_block += t_chunk[d_in] * chunks / cores
+    model_s = N_LAYERS * per_block
+    weights = sum(l[1] * l[2] for l in layers)
+    return {
+        "value": weights / model_s, "unit": "weights/s", "cores": cores, "kind": "port",
+        "seconds_per_model": model_s, "sample_wall_s": wall,
+        "sample": ("CPU oracle (C++ restatement of the reference rayon path, OpenMP, %d threads): factorisation of "
+                   "one 2048- and one 5632-wide Hessian + one 128-row chunk of q_proj and down_proj, extrapolated "
+                   "to 22 decoder layers with row chunks spread over %d cores" % (cores, cores)),
+    }
+
+
+def run_reference_arm(args, torch, rank, world):
+    """`--impl reference`: the reference's CPU path (oracle port: Rust toolchain absent) on the host cores."""
+    if rank != 0:
+        return
+    cfg = bench_config()
+    device = "cuda" if torch.cuda.is_available() else "cpu"
+    layers, inputs = model_layers(1)
+    H = [make_hessian(n, 1000 + i, TOKENS, torch, device) for i, (_, n) in enumerate(inputs)]
+    W = [make_weight(d_out, d_in, 50000 + i, torch, device) for i, (_, d_out, d_in, _) in enumerate(layers)]
+    full_layers, _ = model_layers(N_LAYERS)
+    vals = []
+    res = None
+    for i in range(args.warmup + args.steps):
+        res = cpu_sample(layers, inputs, H, W, cfg)
+        if i >= args.warmup:
+            vals.append(res["seconds_per_model"])
+    sec = statistics.median(vals)
+    weights = sum(l[1] * l[2] for l in full_layers)
+    value = weights / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "weights/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "seconds_per_model": sec,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(cfg),
+        "cpu_baseline": {"value": value, "unit": "weights/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": value, "unit": "weights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is a Rust crate and no Rust toolchain exists on this image; the timed CPU path is "
+                "the C++ restatement of it (oracle/), run with all host threads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg):
+    return {"workload": "TinyLlama-1.1B-shaped model (configs[1]): 22 decoder layers, 154 linear layers, "
+                        "9.69e8 bf16-valued weights, 88 Hessians from 262144 seeded tokens",
+            "bits": cfg.bits, "group": cfg.group, "mse_grid": cfg.mse_grid, "method": cfg.method,
+            "block": cfg.block, "sub_block": cfg.sub_block, "passes": cfg.passes, "tol": cfg.tol,
+            "row_chunk": cfg.row_chunk, "l2": "inputs (W 3.9 GB + H 3.8 GB f32) larger than the 126 MB L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="decoder layers (22 = the configs[1] model)")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+
+    if args.impl == "reference":
+        run_reference_arm(args, torch, rank, world)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    import cdclq
+
+    cdclq.lib()
+    cfg = bench_config()
+    device = "cuda"
+    layers, inputs, H, W = generate(torch, device, args.layers)
+    total_weights = sum(l[1] * l[2] for l in layers)
+    batch = Batch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        batch.run(stream.cuda_stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches0 = cdclq.lib().cdclq_launch_count()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    profiles = []
+    for _ in range(args.steps):
+        batch.run(stream.cuda_stream)
+        profiles.append(cdclq._lib.last_run_profile())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    launches = cdclq.lib().cdclq_launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        # per-layer losses of the row shards are additive: all-reduce the model totals
+        lt = torch.tensor([sum(s.loss_gptq for s in batch.stats), sum(s.loss_final for s in batch.stats)],
+                          dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(lt)
+        loss_gptq, loss_final = float(lt[0]), float(lt[1])
+    else:
+        loss_gptq = sum(s.loss_gptq for s in batch.stats)
+        loss_final = sum(s.loss_final for s in batch.stats)
+
+    # ---- e2e through the public C ABI with pinned host buffers
+    Hh = [h.cpu().pin_memory() for h in H]
+    Wh = [w.cpu().pin_memory() for w in W]
+    hb = Batch(torch, layers, inputs, Hh, Wh, cfg, rank, world, on_device=False)
+    hb.run(0)  # warm the host path once
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        hb.run(0)
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    if rank == 0:
+        prof = profiles[-1]
+        peaks = load_peaks()
+        fp32_peak = fp32_simt_peak_tflops(torch)
+        rep_tflops = prof["flops_repair"] / (prof["ms_repair"] * 1e-3) / 1e12 if prof["ms_repair"] > 0 else 0.0
+        p1_tflops = prof["flops_phase1"] / (prof["ms_phase1"] * 1e-3) / 1e12 if prof["ms_phase1"] > 0 else 0.0
+        line = {
+            "metric": METRIC, "value": total_weights / (ms * 1e-3), "unit": "weights/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "seconds_per_model": ms * 1e-3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded bf16-valued weights and tokens; no checkpoints or datasets offline)",
+            "config": workload_config(cfg),
+            "e2e": {"value": total_weights / e2e_s, "unit": "weights/s", "seconds_per_model": e2e_s,
+                    "h2d_bytes_per_step": hb.h2d_bytes, "d2h_bytes_per_step": hb.d2h_bytes},
+            "gpu_launches": int(launches),
+            "roofline": {
+                "kernel": "repair_pass_kernel (CDCL repair gradients on the FP32 SIMT GEMM core)",
+                "bound": "fp32", "achieved": rep_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
+                "frac": rep_tflops / fp32_peak if fp32_peak else None, "traffic": None,
+                "peak_source": "measured in this run: cuBLAS SGEMM 8192^3 with TF32 off (FFMA); MEASURED_PEAKS.json "
+                               "has no FP32 CUDA-core figure",
+            },
+            "phases_ms": {k: prof[k] for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair", "ms_final")},
+            "phase1_tflops": p1_tflops,
+            "factorisations": prof["factorisations"], "repair_pass_launches": prof["repair_launches"],
+            "loss_gptq": loss_gptq, "loss_final": loss_final,
+            "clocks": clk,
+            "peaks_file": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_sample(layers[:7], inputs[:4], H[:4], W[:7], cfg)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

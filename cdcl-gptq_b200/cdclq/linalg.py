@@ -1,0 +1,42 @@
+"""`linalg.rs` surface over the CUDA library (src/linalg.rs:200-418)."""
+import ctypes
+
+import numpy as np
+
+from ._lib import check, lib
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def cholesky_lower(a, n):
+    """src/linalg.rs:200-276: in place on an n x n f64 array; lower triangle = L."""
+    assert a.dtype == np.float64 and a.flags.c_contiguous and a.size == n * n
+    check(lib().cdclq_cholesky_lower(_p(a), n))
+    return a
+
+
+def tri_inverse_lower(l, n):
+    """src/linalg.rs:284-347."""
+    l = np.ascontiguousarray(l, np.float64)
+    y = np.zeros((n, n), np.float64)
+    check(lib().cdclq_tri_inverse_lower(_p(l), n, _p(y)))
+    return y
+
+
+def upper_chol_of_inverse(h, n):
+    """src/linalg.rs:362-375: U (f32, upper) with H^-1 = U^T U."""
+    h = np.ascontiguousarray(h, np.float64)
+    u = np.zeros((n, n), np.float32)
+    check(lib().cdclq_upper_chol_of_inverse(_p(h), n, _p(u)))
+    return u
+
+
+def gram_accumulate(x, y, t, n, h):
+    """src/linalg.rs:388-418: h (f64, in place) += x^T y over t tokens."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = x if y is x else np.ascontiguousarray(y, np.float32)
+    assert h.dtype == np.float64 and h.flags.c_contiguous
+    check(lib().cdclq_gram_accumulate(_p(x), _p(y), t, n, _p(h)))
+    return h

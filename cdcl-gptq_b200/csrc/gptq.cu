@@ -1,0 +1,197 @@
+// gptq.cu - phase 1: the blocked GPTQ pass with lazy batch updates (src/engine.rs:388-479).
+//
+// One CTA owns up to 64 rows of one layer for the whole pass (rows are independent under the objective,
+// src/engine.rs:9-15).  Per block of B columns:
+//   1. the block w1 = w[:, i1:i2] is staged in shared memory, k-major ([B][65]) so that each row is a column;
+//   2. columns are processed in order.  Four threads share a row: they compute the group grid together at a
+//      group start (min/max split four ways, the 24 MSE clip candidates split four ways), quantize the
+//      column redundantly, and split the rank-1 in-block compensation w1[:, j+1:i2] -= eps * U[j, j+1:i2]
+//      four ways.  The four lanes sit in one warp, so a __syncwarp orders consecutive columns;
+//   3. the deferred compensation w[:, i2:] -= err1 * U[i1:i2, i2:] runs on the FP32 GEMM core
+//      (A = err1 from shared memory, B = U tiles), one subtraction per element per block as in the reference.
+// Outputs per element: code, dequantized value, and eps^2 (consumed by the per-chunk conflict statistics).
+// Every rounding follows src/engine.rs:404-449 and src/quant.rs:40-95 (see common.cuh).
+#include "common.cuh"
+#include "gemm_core.cuh"
+#include "kernels.h"
+
+namespace cdclq {
+
+constexpr int P1_ROWS = 64;
+constexpr int P1_W1LD = 65;  // w1 stride (conflict-free transposed staging)
+constexpr int P1_ELD = GEMM_ALD;  // err1 stride (16-byte aligned k-major A operand)
+
+static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+size_t phase1_smem_bytes(int block) {
+    size_t b = (size_t)block;
+    return align16(b * P1_W1LD * 4) + align16(b * P1_ELD * 4) + align16(b * P1_ROWS) +
+           (size_t)gemm_stage_floats<8>() * 4;
+}
+
+__global__ void __launch_bounds__(256, 1) gptq_phase1_kernel(const P1Item* __restrict__ items, int B, int mse) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const P1Item it = items[blockIdx.x];
+    const int n = it.n, g = it.g, ng = it.ng, rows = it.rows;
+    const int tid = threadIdx.x;
+    const int r = tid >> 2, sub = tid & 3;
+    const bool rvalid = r < rows;
+
+    float* w1 = reinterpret_cast<float*>(smem_raw);
+    float* err1 = reinterpret_cast<float*>(smem_raw + align16((size_t)B * P1_W1LD * 4));
+    uint8_t* cbuf = smem_raw + align16((size_t)B * P1_W1LD * 4) + align16((size_t)B * P1_ELD * 4);
+    float* stage = reinterpret_cast<float*>(cbuf + align16((size_t)B * P1_ROWS));
+
+    float* w = it.w + (int64_t)it.row0 * n;  // tile rows: w[rr * n + c]
+    const float* U = it.u;
+
+    float s = 1.0f, z = 0.0f, maxq = 1.0f;  // current group grid of this thread's row
+    for (int i1 = 0; i1 < n; i1 += B) {
+        const int i2 = min(i1 + B, n), cnt = i2 - i1;
+        for (int idx = tid; idx < P1_ROWS * cnt; idx += blockDim.x) {
+            int rr = idx / cnt, k = idx - rr * cnt;
+            w1[k * P1_W1LD + rr] = (rr < rows) ? w[(int64_t)rr * n + i1 + k] : 0.0f;
+        }
+        for (int idx = tid; idx < P1_ELD * cnt; idx += blockDim.x) err1[idx] = 0.0f;
+        __syncthreads();
+
+        for (int i = 0; i < cnt; i++) {
+            const int j = i1 + i;
+            if (j % g == 0) {
+                // ---- group grid from the weights current at its first column (src/engine.rs:410-423)
+                const int gi = j / g, gend = min(j + g, n);
+                const uint32_t bits = it.gbits[gi];
+                maxq = (float)((1u << bits) - 1u);
+                float xmin = 0.0f, xmax = 0.0f;
+                for (int col = j + sub; col < gend; col += 4) {
+                    float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r] : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+                    xmin = min_sel(xmin, v);
+                    xmax = max_sel(xmax, v);
+                }
+#pragma unroll
+                for (int o = 1; o < 4; o <<= 1) {
+                    xmin = min_sel(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
+                    xmax = max_sel(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+                }
+                if (xmin == 0.0f && xmax == 0.0f) {
+                    xmin = -1.0f;
+                    xmax = 1.0f;
+                }
+                grid_mk(xmin, xmax, maxq, s, z);
+                if (mse) {
+                    float best_err = INFINITY;
+                    int best_i = 24;
+                    for (int ci = sub; ci < 24; ci += 4) {
+                        float p = clip_ratio(ci), cs, cz;
+                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, cs, cz);
+                        float err = 0.0f;
+                        for (int col = j; col < gend; col++) {
+                            float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r]
+                                                 : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+                            uint8_t c;
+                            float d;
+                            quant_code(v, cs, cz, maxq, c, d);
+                            float e = __fsub_rn(d, v);
+                            err = __fadd_rn(err, __fmul_rn(e, e));
+                        }
+                        if (err < best_err) {
+                            best_err = err;
+                            best_i = ci;
+                        }
+                    }
+                    // first index of the strict minimum == min error, ties to the smaller index
+#pragma unroll
+                    for (int o = 1; o < 4; o <<= 1) {
+                        float oe = __shfl_xor_sync(0xffffffffu, best_err, o);
+                        int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+                        if (oe < best_err || (oe == best_err && oi < best_i)) {
+                            best_err = oe;
+                            best_i = oi;
+                        }
+                    }
+                    if (best_i < 24) {
+                        float p = clip_ratio(best_i);
+                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, s, z);
+                    }
+                }
+                if (sub == 0 && rvalid) {
+                    int64_t so = (int64_t)(it.row0 + r) * ng + gi;
+                    it.scales[so] = s;
+                    it.zeros[so] = z;
+                }
+            }
+            // ---- quantize column j and compensate the rest of the block (src/engine.rs:424-448)
+            const float wv = w1[i * P1_W1LD + r];
+            uint8_t c;
+            float dq;
+            quant_code(wv, s, z, maxq, c, dq);
+            const float inv_d = __fdiv_rn(1.0f, __ldg(U + (int64_t)j * n + j));
+            const float e = __fmul_rn(__fsub_rn(wv, dq), inv_d);
+            __syncwarp();
+            if (sub == 0) {
+                err1[i * P1_ELD + r] = e;
+                cbuf[i * P1_ROWS + r] = c;
+                w1[i * P1_W1LD + r] = dq;  // column i is final: keep its dequantized value
+            }
+            const float* urow = U + (int64_t)j * n + i1;
+            for (int k = i + 1 + sub; k < cnt; k += 4) {
+                float* x = &w1[k * P1_W1LD + r];
+                *x = __fsub_rn(*x, __fmul_rn(e, __ldg(urow + k)));
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+
+        // ---- block outputs: codes, dequantized weights, eps^2
+        for (int idx = tid; idx < rows * cnt; idx += blockDim.x) {
+            int rr = idx / cnt, k = idx - rr * cnt;
+            int64_t off = (int64_t)(it.row0 + rr) * n + i1 + k;
+            it.codes[off] = cbuf[k * P1_ROWS + rr];
+            it.wq[off] = w1[k * P1_W1LD + rr];
+            float ev = err1[k * P1_ELD + rr];
+            it.eps2[off] = __fmul_rn(ev, ev);
+        }
+
+        // ---- lazy update of the columns past the block (src/engine.rs:452-471): w -= err1 * U[i1:i2, i2:]
+        if (i2 < n) {
+            const int ty = tid >> 4, tx = tid & 15;
+            for (int c0 = i2; c0 < n; c0 += 128) {
+                float acc[4][8];
+#pragma unroll
+                for (int a = 0; a < 4; a++)
+#pragma unroll
+                    for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
+                BGlobal<8> Bop{U + (int64_t)i1 * n, (int64_t)n, (int64_t)c0, min(128, n - c0), cnt,
+                               (n % 4 == 0) && (c0 % 4 == 0)};
+                gemm_smem_a<8>(acc, err1, Bop, cnt, stage);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    int rr = ty * 4 + a;
+                    if (rr >= rows) continue;
+#pragma unroll
+                    for (int b = 0; b < 8; b++) {
+                        int cc = c0 + ColMap<8>::col(tx, b);
+                        if (cc < n) {
+                            float* p = &w[(int64_t)rr * n + cc];
+                            *p = __fsub_rn(*p, acc[a][b]);
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+int launch_phase1(const P1Item* items_dev, int nitems, int block, int mse, cudaStream_t st) {
+    if (nitems == 0) return 0;
+    size_t smem = phase1_smem_bytes(block);
+    cudaError_t e = cudaFuncSetAttribute(gptq_phase1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "phase1 smem attribute");
+    CDCLQ_LAUNCH(gptq_phase1_kernel, nitems, 256, smem, st, items_dev, block, mse);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "gptq_phase1_kernel launch");
+    return 0;
+}
+
+}  // namespace cdclq

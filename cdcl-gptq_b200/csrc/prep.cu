@@ -1,0 +1,580 @@
+// prep.cu - Hessian preparation and the f64 factorisation H^-1 = U^T U (src/engine.rs:320-342,
+// src/linalg.rs:200-375), batched over the distinct layer inputs of one width.
+//
+// Every element goes through exactly the reference's sequence of roundings:
+//   * permute + dead-diagonal patch + relative damping in f64, the mean of the diagonal summed in order;
+//   * the flip (h.reverse()) is folded into the write of the permuted matrix (hr[n-1-i][n-1-j] = hp[i][j]);
+//   * blocked right-looking Cholesky with NB = 96: the diagonal block and the panel solve are scalar code in
+//     the reference (mul then sub, no FMA) and stay so here; the left-looking dot products of the reference
+//     are applied in the same per-element order (t ascending) as right-looking updates, which exposes the
+//     parallelism without changing a single rounding;
+//   * the trailing update is a GEMM (the unpinned `matrixmultiply` call) in the fixed order: acc = sum_t
+//     fma(.), then a -= acc;
+//   * the triangular inverse: explicit 96-wide diagonal-block inverses (scalar, `acc += l*y`), then
+//     T = L[s:e, :s] Y[:s, :s] and Y[s:e, :s] = -Yii T, both GEMMs in the fixed order.  Terms that multiply
+//     an exact zero of a triangular operand are skipped: the accumulator is never -0, so a zero product is
+//     an exact no-op;
+//   * U[i][j] = (f32) Y[n-1-i][n-1-j] for j >= i.
+// FP64 runs on the SIMT DFMA pipe: on B200 its peak equals the FP64 tensor-core (DMMA) peak, and DMMA would
+// not reproduce the fixed summation order.
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cdclq {
+
+constexpr int NB = 96;  // src/linalg.rs:202 and :285
+
+// ---------------------------------------------------------------------------------------------------------
+// src/engine.rs:321-338: patched diagonal, its mean in order, the damping value
+__global__ void prep_diag_kernel(const PrepItem* __restrict__ items, int n) {
+    const PrepItem it = items[blockIdx.y];
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t p = it.perm[i];
+    double v = (double)it.h[(int64_t)p * n + p];
+    it.dg[i] = (v == 0.0) ? 1.0 : v;
+}
+
+__global__ void prep_mean_kernel(const PrepItem* __restrict__ items, int n, double damp) {
+    const PrepItem it = items[blockIdx.x];
+    if (threadIdx.x != 0) return;
+    double s = 0.0;
+    for (int i = 0; i < n; i++) s = __dadd_rn(s, it.dg[i]);
+    double mean = __ddiv_rn(s, (double)n);
+    *it.damp_val = __dmul_rn(damp, mean);
+    it.status->err = 0;
+    it.status->pivot = -1;
+    it.status->value = 0.0;
+}
+
+// hp[a][b] = (f64) h[perm a][perm b], diagonal patched and damped; h32 = (f32) hp; hr = flip(hp)
+__global__ void prep_fill_kernel(const PrepItem* __restrict__ items, int n) {
+    const PrepItem it = items[blockIdx.z];
+    int a = blockIdx.y;
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    double v;
+    if (a == b)
+        v = __dadd_rn(it.dg[a], *it.damp_val);
+    else
+        v = (double)it.h[(int64_t)it.perm[a] * n + it.perm[b]];
+    it.h32[(int64_t)a * n + b] = (float)v;
+    it.hr[(int64_t)(n - 1 - a) * n + (n - 1 - b)] = v;
+}
+
+int launch_prepare(const PrepItem* items_dev, int nitems, int n, double damp, cudaStream_t st) {
+    if (nitems == 0) return 0;
+    dim3 g1((n + 255) / 256, nitems);
+    CDCLQ_LAUNCH(prep_diag_kernel, g1, 256, 0, st, items_dev, n);
+    CDCLQ_LAUNCH(prep_mean_kernel, nitems, 32, 0, st, items_dev, n, damp);
+    dim3 g2((n + 255) / 256, n, nitems);
+    CDCLQ_LAUNCH(prep_fill_kernel, g2, 256, 0, st, items_dev, n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "prepare kernels launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Cholesky step 1 (src/linalg.rs:209-229): the kb x kb diagonal block, one CTA per matrix.
+// Right-looking form of the reference's left-looking loops: after column t is final, every later element
+// (i, c) of the block, c <= i, receives its `- a[i][t]*a[c][t]` term - the same terms in the same order.
+struct CholArgs {
+    double* a;
+    FactorStatus* status;
+};
+
+__global__ void __launch_bounds__(256) chol_diag_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    extern __shared__ double sblk[];  // [kb][kb+1]
+    const CholArgs ar = args[blockIdx.x];
+    if (ar.status->err) return;
+    const int ld = kb + 1, tid = threadIdx.x, nt = blockDim.x;
+    double* A = ar.a;
+    for (int idx = tid; idx < kb * kb; idx += nt) {
+        int i = idx / kb, c = idx - i * kb;
+        if (c <= i) sblk[i * ld + c] = A[(int64_t)(k + i) * n + (k + c)];
+    }
+    __shared__ int bad;
+    __shared__ double dj;
+    if (tid == 0) bad = 0;
+    __syncthreads();
+    for (int j = 0; j < kb; j++) {
+        if (tid == 0) {
+            double d = sblk[j * ld + j];
+            if (!(d > 0.0) || !isfinite(d)) {
+                bad = 1;
+                ar.status->err = 1;
+                ar.status->pivot = k + j;
+                ar.status->value = d;
+            } else {
+                d = __dsqrt_rn(d);
+                sblk[j * ld + j] = d;
+                dj = d;
+            }
+        }
+        __syncthreads();
+        if (bad) return;
+        const double d = dj;
+        for (int i = j + 1 + tid; i < kb; i += nt) sblk[i * ld + j] = __ddiv_rn(sblk[i * ld + j], d);
+        __syncthreads();
+        // pairs (i, c) with j < c <= i < kb, enumerated as i = j+1+pi, c = j+1+pc, pc <= pi
+        const int m = kb - j - 1;
+        const int npairs = m * (m + 1) / 2;
+        for (int p = tid; p < npairs; p += nt) {
+            int pi = (int)((sqrt(8.0 * p + 1.0) - 1.0) * 0.5);
+            while ((pi + 1) * (pi + 2) / 2 <= p) pi++;
+            while (pi * (pi + 1) / 2 > p) pi--;
+            int pc = p - pi * (pi + 1) / 2;
+            int i = j + 1 + pi, c = j + 1 + pc;
+            sblk[i * ld + c] = __dsub_rn(sblk[i * ld + c], __dmul_rn(sblk[i * ld + j], sblk[c * ld + j]));
+        }
+        __syncthreads();
+    }
+    for (int idx = tid; idx < kb * kb; idx += nt) {
+        int i = idx / kb, c = idx - i * kb;
+        if (c <= i) A[(int64_t)(k + i) * n + (k + c)] = sblk[i * ld + c];
+    }
+}
+
+// Cholesky step 2 (src/linalg.rs:232-241): panel rows i >= kend solve X L_kk^T = A_panel.  One warp per row,
+// lane l owns columns l, l+32, l+64; the reference's per-row loop `s -= row[t]*top[j][t]; row[j] = s/top[j][j]`
+// becomes: row[j] final -> broadcast -> row[c] -= row[j] * L[c][j] for c > j (same per-element order).
+__global__ void __launch_bounds__(256) chol_panel_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    extern __shared__ double lt[];  // [kb][kb]: lt[j][c] = L[k+c][k+j] (c >= j), the transposed block
+    const CholArgs ar = args[blockIdx.y];
+    if (ar.status->err) return;
+    double* A = ar.a;
+    const int kend = k + kb;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int idx = tid; idx < kb * kb; idx += blockDim.x) {
+        int c = idx / kb, j = idx - c * kb;
+        lt[j * kb + c] = (j <= c) ? A[(int64_t)(k + c) * n + (k + j)] : 0.0;
+    }
+    __syncthreads();
+    const int rows_per_cta = 64;
+    const int rbeg = kend + blockIdx.x * rows_per_cta;
+    for (int rr = warp; rr < rows_per_cta; rr += 8) {
+        const int i = rbeg + rr;
+        if (i >= n) break;
+        double* row = A + (int64_t)i * n + k;
+        double x0 = (lane < kb) ? row[lane] : 0.0;
+        double x1 = (lane + 32 < kb) ? row[lane + 32] : 0.0;
+        double x2 = (lane + 64 < kb) ? row[lane + 64] : 0.0;
+        for (int j = 0; j < kb; j++) {
+            const int owner = j & 31, slot = j >> 5;
+            double xj;
+            if (lane == owner) {
+                double v = slot == 0 ? x0 : (slot == 1 ? x1 : x2);
+                v = __ddiv_rn(v, lt[j * kb + j]);
+                if (slot == 0) x0 = v; else if (slot == 1) x1 = v; else x2 = v;
+                xj = v;
+            }
+            xj = __shfl_sync(0xffffffffu, xj, owner);
+            const double* lrow = lt + j * kb;
+            int c0 = lane, c1 = lane + 32, c2 = lane + 64;
+            if (c0 > j && c0 < kb) x0 = __dsub_rn(x0, __dmul_rn(xj, lrow[c0]));
+            if (c1 > j && c1 < kb) x1 = __dsub_rn(x1, __dmul_rn(xj, lrow[c1]));
+            if (c2 > j && c2 < kb) x2 = __dsub_rn(x2, __dmul_rn(xj, lrow[c2]));
+        }
+        if (lane < kb) row[lane] = x0;
+        if (lane + 32 < kb) row[lane + 32] = x1;
+        if (lane + 64 < kb) row[lane + 64] = x2;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// f64 GEMM tile (64 x 64 outputs, 256 threads, 4 x 4 per thread, K staged 8 at a time).  Thread (ty, tx)
+// owns rows ty*4..ty*4+3 and columns tx*4..tx*4+3.  Operands are fetched through callables so that the
+// trailing update, T = L Y and -Yii T share one core.  acc receives the products in increasing k.
+constexpr int DKT = 8;
+constexpr int DLD = 68;
+
+// B_ALONG_K: the B operand is contiguous along k in memory (B(k, c) = P[c][k]); otherwise along c.
+template <bool B_ALONG_K, class FA, class FB>
+__device__ __forceinline__ void dgemm_tile(double (&acc)[4][4], FA fa, FB fb, int kbeg, int kend, double* As,
+                                           double* Bs) {
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    for (int k0 = kbeg; k0 < kend; k0 += DKT) {
+        // stage: 64 rows x 8 k of A and 8 k x 64 cols of B (512 each -> 2 per thread), each fetched along its
+        // contiguous memory direction
+        for (int q = tid; q < 64 * DKT; q += 256) {
+            int r = q / DKT, kk = q - r * DKT;
+            int k = k0 + kk;
+            As[kk * DLD + r] = (k < kend) ? fa(r, k) : 0.0;
+            int c, kb2;
+            if (B_ALONG_K) {
+                c = q / DKT;
+                kb2 = q - c * DKT;
+            } else {
+                c = q & 63;
+                kb2 = q >> 6;
+            }
+            int k2 = k0 + kb2;
+            Bs[kb2 * DLD + c] = (k2 < kend) ? fb(k2, c) : 0.0;
+        }
+        __syncthreads();
+        int kn = min(DKT, kend - k0);
+        for (int kk = 0; kk < kn; kk++) {
+            double2 a01 = *reinterpret_cast<const double2*>(As + kk * DLD + ty * 4);
+            double2 a23 = *reinterpret_cast<const double2*>(As + kk * DLD + ty * 4 + 2);
+            double2 b01 = *reinterpret_cast<const double2*>(Bs + kk * DLD + tx * 4);
+            double2 b23 = *reinterpret_cast<const double2*>(Bs + kk * DLD + tx * 4 + 2);
+            double av[4] = {a01.x, a01.y, a23.x, a23.y};
+            double bv[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fma_rn(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+}
+
+// Cholesky step 3 (src/linalg.rs:242-271): A22[i][c] -= sum_t P[i][t] P[c][t] for kend <= c <= i < n,
+// lower 64x64 tiles only (the reference also updates some upper-triangle garbage that is never read).
+__global__ void __launch_bounds__(256) chol_trail_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    __shared__ __align__(16) double As[DKT * DLD];
+    __shared__ __align__(16) double Bs[DKT * DLD];
+    const CholArgs ar = args[blockIdx.y];
+    if (ar.status->err) return;
+    double* A = ar.a;
+    const int kend = k + kb;
+    // tile index -> (ti, tc), tc <= ti
+    const long long x = blockIdx.x;
+    int ti = (int)((sqrt(8.0 * (double)x + 1.0) - 1.0) * 0.5);
+    while ((long long)(ti + 1) * (ti + 2) / 2 <= x) ti++;
+    while ((long long)ti * (ti + 1) / 2 > x) ti--;
+    const int tc = (int)(x - (long long)ti * (ti + 1) / 2);
+    const int r0 = kend + ti * 64, c0 = kend + tc * 64;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    auto fa = [&](int r, int t) -> double {
+        int i = r0 + r;
+        return (i < n) ? A[(int64_t)i * n + k + t] : 0.0;
+    };
+    auto fb = [&](int t, int c) -> double {
+        int cc = c0 + c;
+        return (cc < n) ? A[(int64_t)cc * n + k + t] : 0.0;
+    };
+    dgemm_tile<true>(acc, fa, fb, 0, kb, As, Bs);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        int i = r0 + ty * 4 + a;
+        if (i >= n) continue;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int c = c0 + tx * 4 + b;
+            if (c <= i) {
+                double* p = A + (int64_t)i * n + c;
+                *p = __dsub_rn(*p, acc[a][b]);
+            }
+        }
+    }
+}
+
+static int run_cholesky(const CholArgs* args_dev, int nitems, int n, cudaStream_t st) {
+    for (int k = 0; k < n; k += NB) {
+        int kb = min(NB, n - k);
+        int kend = k + kb;
+        size_t smem1 = (size_t)kb * (kb + 1) * sizeof(double);
+        cudaFuncSetAttribute(chol_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 256, smem1, st, args_dev, n, k, kb);
+        if (kend < n) {
+            int rows_below = n - kend;
+            size_t smem2 = (size_t)kb * kb * sizeof(double);
+            cudaFuncSetAttribute(chol_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+            dim3 gp((rows_below + 63) / 64, nitems);
+            CDCLQ_LAUNCH(chol_panel_kernel, gp, 256, smem2, st, args_dev, n, k, kb);
+            long long T = (rows_below + 63) / 64;
+            dim3 gt((unsigned)(T * (T + 1) / 2), nitems);
+            CDCLQ_LAUNCH(chol_trail_kernel, gt, 256, 0, st, args_dev, n, k, kb);
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "cholesky kernels launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Triangular inverse step 1 (src/linalg.rs:292-306): explicit inverse of the w x w diagonal block.
+// Thread c computes column c by forward substitution: y_c = 1/l_cc; y_t = -acc_t / l_tt with
+// acc_t = sum_{t'=c}^{t-1} l[t][t'] y_t' accumulated as `acc += l*y` from 0.0 in increasing t'.
+struct TriArgs {
+    const double* l;
+    double* y;
+    double* t;
+    FactorStatus* status;
+};
+
+__global__ void __launch_bounds__(128) tri_diag_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
+    extern __shared__ double tsm[];
+    const TriArgs ar = args[blockIdx.x];
+    if (ar.status->err) return;
+    double* Ls = tsm;                 // [w][w] lower block
+    double* Acc = tsm + (size_t)w * w;  // [w][w+1]: Acc[i][c]
+    const int ldc = w + 1, tid = threadIdx.x;
+    for (int idx = tid; idx < w * w; idx += blockDim.x) {
+        int i = idx / w, c = idx - i * w;
+        Ls[idx] = (c <= i) ? ar.l[(int64_t)(s + i) * n + (s + c)] : 0.0;
+        Acc[i * ldc + c] = 0.0;
+    }
+    __syncthreads();
+    const int c = tid;
+    if (c < w) {
+        for (int t = c; t < w; t++) {
+            double yt = (t == c) ? __ddiv_rn(1.0, Ls[t * w + t]) : __ddiv_rn(-Acc[t * ldc + c], Ls[t * w + t]);
+            Acc[t * ldc + c] = yt;  // column c, row t is now final
+            for (int i = t + 1; i < w; i++)
+                Acc[i * ldc + c] = __dadd_rn(Acc[i * ldc + c], __dmul_rn(Ls[i * w + t], yt));
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < w * w; idx += blockDim.x) {
+        int i = idx / w, cc = idx - i * w;
+        if (cc <= i) ar.y[(int64_t)(s + i) * n + (s + cc)] = Acc[i * ldc + cc];
+    }
+}
+
+// Triangular inverse step 2 (src/linalg.rs:307-325): T[i][j] = sum_k L[s+i][k] Y[k][j], k in [0, s).
+// Y is lower triangular: for the column tile starting at j0 every k < j0 multiplies an exact zero.
+__global__ void __launch_bounds__(256) tri_gemm1_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
+    __shared__ __align__(16) double As[DKT * DLD];
+    __shared__ __align__(16) double Bs[DKT * DLD];
+    const TriArgs ar = args[blockIdx.z];
+    if (ar.status->err) return;
+    const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    const double* L = ar.l;
+    const double* Y = ar.y;
+    auto fa = [&](int r, int k) -> double {
+        int i = i0 + r;
+        return (i < w) ? L[(int64_t)(s + i) * n + k] : 0.0;
+    };
+    auto fb = [&](int k, int c) -> double {
+        int j = j0 + c;
+        return (j < s) ? Y[(int64_t)k * n + j] : 0.0;
+    };
+    dgemm_tile<false>(acc, fa, fb, j0, s, As, Bs);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        int i = i0 + ty * 4 + a;
+        if (i >= w) continue;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int j = j0 + tx * 4 + b;
+            if (j < s) ar.t[(int64_t)i * n + j] = acc[a][b];
+        }
+    }
+}
+
+// Triangular inverse step 3 (src/linalg.rs:326-341): Y[s+i][j] = -sum_k Yii[i][k] T[k][j], k in [0, w);
+// Yii is lower triangular, so only k <= i contribute.
+__global__ void __launch_bounds__(256) tri_gemm2_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
+    __shared__ __align__(16) double As[DKT * DLD];
+    __shared__ __align__(16) double Bs[DKT * DLD];
+    const TriArgs ar = args[blockIdx.z];
+    if (ar.status->err) return;
+    const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    double* Y = ar.y;
+    const double* T = ar.t;
+    auto fa = [&](int r, int k) -> double {
+        int i = i0 + r;
+        return (i < w && k <= i) ? Y[(int64_t)(s + i) * n + (s + k)] : 0.0;
+    };
+    auto fb = [&](int k, int c) -> double {
+        int j = j0 + c;
+        return (j < s) ? T[(int64_t)k * n + j] : 0.0;
+    };
+    int kend = min(w, i0 + 64);
+    dgemm_tile<false>(acc, fa, fb, 0, kend, As, Bs);
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        int i = i0 + ty * 4 + a;
+        if (i >= w) continue;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int j = j0 + tx * 4 + b;
+            if (j < s) Y[(int64_t)(s + i) * n + j] = -acc[a][b];
+        }
+    }
+}
+
+static int run_tri_inverse(const TriArgs* args_dev, int nitems, int n, cudaStream_t st) {
+    for (int s = 0; s < n; s += NB) {
+        int w = min(NB, n - s);
+        size_t smem = (size_t)w * w * sizeof(double) + (size_t)w * (w + 1) * sizeof(double);
+        cudaFuncSetAttribute(tri_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        CDCLQ_LAUNCH(tri_diag_kernel, nitems, 128, smem, st, args_dev, n, s, w);
+        if (s > 0) {
+            dim3 g((s + 63) / 64, (w + 63) / 64, nitems);
+            CDCLQ_LAUNCH(tri_gemm1_kernel, g, 256, 0, st, args_dev, n, s, w);
+            CDCLQ_LAUNCH(tri_gemm2_kernel, g, 256, 0, st, args_dev, n, s, w);
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "triangular inverse kernels launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// src/linalg.rs:368-373: U[i][j] = (f32) Y[n-1-i][n-1-j] for j >= i, else 0
+__global__ void u_scatter_kernel(const PrepItem* __restrict__ items, int n) {
+    const PrepItem it = items[blockIdx.z];
+    if (it.status->err) return;
+    int i = blockIdx.y;
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    it.u[(int64_t)i * n + j] = (j >= i) ? (float)it.y[(int64_t)(n - 1 - i) * n + (n - 1 - j)] : 0.0f;
+}
+
+// The batched launchers build per-item argument tables in device memory carved from the items' own
+// scratch: the host passes PrepItem tables, the factorisation kernels need (a, status) and (l, y, t, status).
+__global__ void make_chol_args_kernel(const PrepItem* items, CholArgs* chol, TriArgs* tri, int nitems) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nitems) return;
+    chol[i].a = items[i].hr;
+    chol[i].status = items[i].status;
+    tri[i].l = items[i].hr;
+    tri[i].y = items[i].y;
+    tri[i].t = items[i].tbuf;
+    tri[i].status = items[i].status;
+}
+
+struct ArgTables {
+    CholArgs* chol = nullptr;
+    TriArgs* tri = nullptr;
+};
+
+static int make_tables(const PrepItem* items_dev, int nitems, cudaStream_t st, ArgTables& t) {
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&t.chol, sizeof(CholArgs) * nitems, st));
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&t.tri, sizeof(TriArgs) * nitems, st));
+    CDCLQ_LAUNCH(make_chol_args_kernel, (nitems + 127) / 128, 128, 0, st, items_dev, t.chol, t.tri, nitems);
+    return 0;
+}
+
+static void free_tables(ArgTables& t, cudaStream_t st) {
+    if (t.chol) cudaFreeAsync(t.chol, st);
+    if (t.tri) cudaFreeAsync(t.tri, st);
+    t.chol = nullptr;
+    t.tri = nullptr;
+}
+
+int launch_cholesky(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
+    ArgTables t;
+    int rc = make_tables(items_dev, nitems, st, t);
+    if (!rc) rc = run_cholesky(t.chol, nitems, n, st);
+    free_tables(t, st);
+    return rc;
+}
+
+int launch_tri_inverse(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
+    ArgTables t;
+    int rc = make_tables(items_dev, nitems, st, t);
+    if (!rc) rc = run_tri_inverse(t.tri, nitems, n, st);
+    free_tables(t, st);
+    return rc;
+}
+
+int launch_u_scatter(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
+    dim3 g((n + 255) / 256, n, nitems);
+    CDCLQ_LAUNCH(u_scatter_kernel, g, 256, 0, st, items_dev, n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "u_scatter_kernel launch");
+}
+
+// Single-matrix entry points for the C ABI (cholesky_lower / tri_inverse_lower on their own).
+int device_cholesky(double* a, int n, FactorStatus* status, cudaStream_t st) {
+    CholArgs* args = nullptr;
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&args, sizeof(CholArgs), st));
+    CholArgs h{a, status};
+    cudaError_t e = cudaMemcpyAsync(args, &h, sizeof h, cudaMemcpyHostToDevice, st);
+    int rc = (e == cudaSuccess) ? 0 : cuda_error(e, "cholesky args");
+    if (!rc) rc = run_cholesky(args, 1, n, st);
+    cudaStreamSynchronize(st);
+    cudaFreeAsync(args, st);
+    return rc;
+}
+
+int device_tri_inverse(const double* l, double* y, double* tbuf, int n, cudaStream_t st) {
+    TriArgs* args = nullptr;
+    FactorStatus* status = nullptr;
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&args, sizeof(TriArgs), st));
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&status, sizeof(FactorStatus), st));
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(FactorStatus), st));
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(y, 0, sizeof(double) * (size_t)n * n, st));
+    TriArgs h{l, y, tbuf, status};
+    cudaError_t e = cudaMemcpyAsync(args, &h, sizeof h, cudaMemcpyHostToDevice, st);
+    int rc = (e == cudaSuccess) ? 0 : cuda_error(e, "tri args");
+    if (!rc) rc = run_tri_inverse(args, 1, n, st);
+    cudaStreamSynchronize(st);
+    cudaFreeAsync(args, st);
+    cudaFreeAsync(status, st);
+    return rc;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Weight-side preparation
+__global__ void hdiag_kernel(const float* h, int n, double* hdiag) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) hdiag[j] = (double)h[(int64_t)j * n + j];
+}
+
+int launch_hdiag(const float* h, int n, double* hdiag, cudaStream_t st) {
+    CDCLQ_LAUNCH(hdiag_kernel, (n + 255) / 256, 256, 0, st, h, n, hdiag);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "hdiag_kernel launch");
+}
+
+// src/engine.rs:279-285 over the dead-zeroed weights: rows summed in order, (w as f64) * (w as f64)
+__global__ void colsq_kernel(const float* w, const double* hdiag, int d_out, int n, double* colsq) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    bool dead = hdiag[j] == 0.0;
+    double s = 0.0;
+    for (int r = 0; r < d_out; r++) {
+        double v = dead ? 0.0 : (double)w[(int64_t)r * n + j];
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    colsq[j] = s;
+}
+
+int launch_colsq(const float* w, const double* hdiag, int d_out, int n, double* colsq, cudaStream_t st) {
+    CDCLQ_LAUNCH(colsq_kernel, (n + 255) / 256, 256, 0, st, w, hdiag, d_out, n, colsq);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "colsq_kernel launch");
+}
+
+__global__ void permute_w_kernel(const float* w, const double* hdiag, const uint32_t* perm, int d_out, int n,
+                                 float* wt) {
+    int r = blockIdx.y;
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n || r >= d_out) return;
+    uint32_t p = perm[j];
+    wt[(int64_t)r * n + j] = (hdiag[p] == 0.0) ? 0.0f : w[(int64_t)r * n + p];
+}
+
+int launch_permute_w(const float* w, const double* hdiag, const uint32_t* perm, int d_out, int n, float* wt,
+                     cudaStream_t st) {
+    for (int r0 = 0; r0 < d_out; r0 += 65535) {
+        int rows = min(65535, d_out - r0);
+        dim3 g((n + 255) / 256, rows);
+        CDCLQ_LAUNCH(permute_w_kernel, g, 256, 0, st, w + (int64_t)r0 * n, hdiag, perm, rows, n, wt + (int64_t)r0 * n);
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "permute_w_kernel launch");
+}
+
+}  // namespace cdclq

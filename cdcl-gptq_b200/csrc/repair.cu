@@ -1,0 +1,442 @@
+// repair.cu - phase 2: conflict selection and the monotone CDCL repair (src/engine.rs:478-671).
+//
+// Work decomposition.  The reference runs phase 2 per row chunk (rc rows): conflict selection sums eps^2
+// over the chunk's rows and the `tol` stop is decided per chunk (src/engine.rs:499-508, 663).  Inside one pass
+// every move (scale refit of a (row, group), code move of a (row, column)) depends only on its own row, so a
+// pass is launched over row SLICES of up to 64 rows; a chunk's slices are reduced in order by a small
+// pass-end kernel that updates the chunk's loss bookkeeping and its stop flag.  Chunks that stopped make
+// every later pass launch a no-op for their slices, which reproduces the per-chunk `break`.
+//
+// Inside a slice CTA (256 threads):
+//   * the block gradients G = E H[:, c0:c1] run on the FP32 GEMM core (fixed k order, bit-exact);
+//   * the sequential per-row work (refit numerators/denominators, the coordinate sweep with its rank-1
+//     gradient updates) runs one thread per row, in the reference's order, on shared-memory tiles.
+#include "common.cuh"
+#include "gemm_core.cuh"
+#include "kernels.h"
+
+namespace cdclq {
+
+constexpr int RP_ROWS = 64;
+constexpr int RP_LD = 68;  // [col][row] tiles (16-byte aligned rows)
+
+static __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// ---------------------------------------------------------------------------------------------------------
+// Per-chunk statistics after phase 1: colloss (rows summed in order), loss_gptq, sub-block sums, conflict
+// selection (src/engine.rs:478-511), and E = W - W_hat (src/engine.rs:516-519).
+__global__ void __launch_bounds__(256) chunk_stats_kernel(const ChunkInfo* __restrict__ chunks, RepairParams rp) {
+    const ChunkInfo ci = chunks[blockIdx.x];
+    const int n = ci.n, rows = ci.rows, tid = threadIdx.x, nt = blockDim.x;
+    const float* eps2 = ci.e;
+    for (int j = tid; j < n; j += nt) {
+        double cl = 0.0;
+        for (int r = 0; r < rows; r++) cl = __dadd_rn(cl, (double)eps2[(int64_t)r * n + j]);
+        ci.colloss[j] = cl;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double lg = 0.0;
+        for (int j = 0; j < n; j++) lg = __dadd_rn(lg, ci.colloss[j]);
+        ci.st->loss_gptq = lg;
+        ci.st->loss_delta = 0.0;
+        ci.st->prev_delta = 0.0;
+        ci.st->updates = 0ull;
+        ci.st->passes = 0;
+        ci.st->n_sel = 0;
+        // a chunk with nothing to repair never enters a pass
+        ci.st->done = (rp.method_cdcl && (rp.do_cd || rp.do_refit)) ? 0 : 1;
+    }
+    const int sbw = ci.sbw, n_sb = ci.n_sb;
+    for (int s = tid; s < n_sb; s += nt) {
+        int c0 = s * sbw, c1 = min(c0 + sbw, n);
+        double acc = 0.0;
+        for (int j = c0; j < c1; j++) acc = __dadd_rn(acc, ci.colloss[j]);
+        ci.sbsum[s] = acc;
+    }
+    __syncthreads();
+    if (rp.method_cdcl && rp.do_cd) {
+        // rank of each sub-block in (descending loss, ascending index) order; the k best are selected and
+        // kept in ascending index order (src/engine.rs:506-509)
+        for (int s = tid; s < n_sb; s += nt) {
+            double v = ci.sbsum[s];
+            int rank = 0;
+            for (int s2 = 0; s2 < n_sb; s2++) {
+                double v2 = ci.sbsum[s2];
+                rank += (v2 > v || (v2 == v && s2 < s)) ? 1 : 0;
+            }
+            ci.sel[s] = (rank < ci.k_sel) ? 1 : 0;  // flag first, compacted below
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int cnt = 0;
+            for (int s = 0; s < n_sb; s++)
+                if (ci.sel[s]) ci.sel[cnt++] = s;  // in place: cnt <= s
+            ci.st->n_sel = cnt;
+        }
+    }
+    __syncthreads();
+    if (rp.method_cdcl && (rp.do_cd || rp.do_refit)) {
+        int64_t total = (int64_t)rows * n;
+        for (int64_t i = tid; i < total; i += nt) ci.e[i] = __fsub_rn(ci.wt[i], ci.wq[i]);
+    }
+}
+
+int launch_chunk_stats(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, cudaStream_t st) {
+    if (nchunks == 0) return 0;
+    CDCLQ_LAUNCH(chunk_stats_kernel, nchunks, 256, 0, st, chunks_dev, rp);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "chunk_stats_kernel launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// A operand of the u H_CC product: A[k][row] = codes[k][row] - z[row] (src/engine.rs:553-558), staged from the
+// shared-memory code tile.
+struct ACodes {
+    const uint8_t* cs;  // [K][RP_ROWS]
+    const float* zr;    // [RP_ROWS]
+    int rows_valid;
+    int K;
+    __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[4]) const {
+        int row = tid >> 2, q = tid & 3;
+        int k = k0 + q * 4;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            r[i] = (row < rows_valid && k + i < K) ? __fsub_rn((float)cs[(k + i) * RP_ROWS + row], zr[row]) : 0.0f;
+    }
+    __device__ __forceinline__ void store(float* As, int tid, const float (&r)[4]) const {
+        int row = tid >> 2, q = tid & 3;
+#pragma unroll
+        for (int i = 0; i < 4; i++) As[(q * 4 + i) * GEMM_ALD + row] = r[i];
+    }
+};
+
+// out[c][row] = (A B)[row][c] for c < wd (wd <= 128), via the widest fitting tile.  Ends synchronised.
+template <class AL>
+__device__ void gemm_to_tile(const AL& A, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
+                             float* stage) {
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const bool vec = (ldb % 4 == 0) && (col0 % 4 == 0);
+    if (wd > 64) {
+        float acc[4][8];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) acc[a][c] = 0.0f;
+        BGlobal<8> Bop{b, ldb, col0, wd, K, vec};
+        gemm_loader_a<8>(acc, A, Bop, K, stage);
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                int cc = ColMap<8>::col(tx, c);
+                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
+            }
+    } else if (wd > 32) {
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
+        BGlobal<4> Bop{b, ldb, col0, wd, K, vec};
+        gemm_loader_a<4>(acc, A, Bop, K, stage);
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                int cc = ColMap<4>::col(tx, c);
+                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
+            }
+    } else {
+        float acc[4][2];
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) acc[a][c] = 0.0f;
+        BGlobal<2> Bop{b, ldb, col0, wd, K, false};
+        gemm_loader_a<2>(acc, A, Bop, K, stage);
+#pragma unroll
+        for (int a = 0; a < 4; a++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                int cc = ColMap<2>::col(tx, c);
+                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
+            }
+    }
+    __syncthreads();
+}
+
+// Shared-memory layout of the repair kernel: a body shared by the refit (group code tile + one 128-column
+// result tile) and the coordinate descent (sub-block code tile, gradient tile, W_hat tile), per-row scalars,
+// then the GEMM staging buffers.
+struct RepairLayout {
+    size_t body, zrow, snew, accept, rowdelta, upd, stage, total;
+};
+
+static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
+    RepairLayout L;
+    size_t gcap = (size_t)(g < 1024 ? g : 1024);
+    size_t refit = al16(gcap * RP_ROWS) + al16((size_t)128 * RP_LD * 4);
+    size_t cd = al16((size_t)sbw * RP_ROWS) + 2 * al16((size_t)sbw * RP_LD * 4);
+    L.body = refit > cd ? refit : cd;
+    L.zrow = L.body;
+    L.snew = L.zrow + RP_ROWS * 4;
+    L.accept = L.snew + RP_ROWS * 4;
+    L.rowdelta = L.accept + RP_ROWS * 4;
+    L.upd = L.rowdelta + RP_ROWS * 8;
+    L.stage = L.upd + RP_ROWS * 8;
+    L.total = L.stage + (size_t)gemm_stage_floats<8>() * 4;
+    return L;
+}
+
+size_t repair_smem_bytes(int g, int sbw) { return repair_layout(g, sbw).total; }
+
+// ---------------------------------------------------------------------------------------------------------
+// One repair pass (or the final refit) over a row slice.
+__global__ void __launch_bounds__(256) repair_pass_kernel(const ChunkInfo* __restrict__ chunks,
+                                                          const SliceItem* __restrict__ slices,
+                                                          SliceAcc* __restrict__ acc_out, RepairParams rp) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const SliceItem sl = slices[blockIdx.x];
+    const ChunkInfo ci = chunks[sl.chunk];
+    const int tid = threadIdx.x;
+    if (!rp.final_refit && ci.st->done) return;  // this chunk has converged (src/engine.rs:663-665)
+
+    const int n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw, rs = sl.rs;
+    const int64_t rbase = (int64_t)sl.r0 * n;   // element offset of the slice inside the chunk
+    const int64_t gbase = (int64_t)sl.r0 * ng;
+    float* E = ci.e + rbase;
+    float* WQ = ci.wq + rbase;
+    uint8_t* CODES = ci.codes + rbase;
+    float* SC = ci.scales + gbase;
+    const float* ZR = ci.zeros + gbase;
+    const float* H = ci.h;
+
+    const size_t gcap = (size_t)(g < 1024 ? g : 1024);
+    const RepairLayout L = repair_layout(g, sbw);
+    float* zrow = reinterpret_cast<float*>(smem_raw + L.zrow);        // [64] zero point of the group
+    float* snew = reinterpret_cast<float*>(smem_raw + L.snew);        // [64] accepted new scale
+    int* accept = reinterpret_cast<int*>(smem_raw + L.accept);        // [64]
+    double* rowdelta = reinterpret_cast<double*>(smem_raw + L.rowdelta);
+    unsigned long long* upd_s = reinterpret_cast<unsigned long long*>(smem_raw + L.upd);
+    float* stage = reinterpret_cast<float*>(smem_raw + L.stage);
+
+    double my_delta = 0.0;            // thread r < rs: this row's accepted loss deltas
+    unsigned long long my_upd = 0ull;
+
+    // ---- closed-form scale refit of every (row, group), groups in order (src/engine.rs:534-589)
+    if (rp.do_refit) {
+        uint8_t* cs = smem_raw;                                              // [gcap][64] codes of the group
+        float* tile = reinterpret_cast<float*>(smem_raw + al16(gcap * RP_ROWS));  // [128][68] G, then u H_CC
+        for (int gi = 0; gi < ng; gi++) {
+            const int c0 = gi * g, wd = min(g, n - c0);
+            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+                int rr = idx / wd, k = idx - rr * wd;
+                cs[k * RP_ROWS + rr] = CODES[(int64_t)rr * n + c0 + k];
+            }
+            if (tid < RP_ROWS) zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
+            __syncthreads();
+            // num = sum_k u_k * G_k, G = E H[:, c0:c1]
+            float num = 0.0f, den = 0.0f;
+            for (int t0 = 0; t0 < wd; t0 += 128) {
+                int wt = min(128, wd - t0);
+                AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
+                gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, tile, stage);
+                if (tid < rs) {
+                    float zr = zrow[tid];
+                    for (int k = 0; k < wt; k++) {
+                        float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
+                        num = __fadd_rn(num, __fmul_rn(u, tile[k * RP_LD + tid]));
+                    }
+                }
+                __syncthreads();
+            }
+            // den = sum_k u_k * (u H_CC)_k
+            for (int t0 = 0; t0 < wd; t0 += 128) {
+                int wt = min(128, wd - t0);
+                ACodes A{cs, zrow, rs, wd};
+                gemm_to_tile(A, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0), wt, wd, tile, stage);
+                if (tid < rs) {
+                    float zr = zrow[tid];
+                    for (int k = 0; k < wt; k++) {
+                        float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
+                        den = __fadd_rn(den, __fmul_rn(u, tile[k * RP_LD + tid]));
+                    }
+                }
+                __syncthreads();
+            }
+            if (tid < RP_ROWS) accept[tid] = 0;
+            if (tid < rs) {
+                if (den > 1e-30f) {
+                    float s_old = SC[(int64_t)tid * ng + gi];
+                    float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
+                    if (!(s_new >= kF16MinNormal)) s_new = kF16MinNormal;  // f32::max(x, MIN)
+                    float d = __fsub_rn(s_new, s_old);
+                    float dlf = __fadd_rn(__fmul_rn(__fmul_rn(-2.0f, d), num), __fmul_rn(__fmul_rn(d, d), den));
+                    double dl = (double)dlf;
+                    if (dl < 0.0) {
+                        SC[(int64_t)tid * ng + gi] = s_new;
+                        snew[tid] = s_new;
+                        accept[tid] = 1;
+                        my_delta = __dadd_rn(my_delta, dl);
+                        my_upd++;
+                    }
+                }
+            }
+            __syncthreads();
+            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+                int rr = idx / wd, k = idx - rr * wd;
+                if (accept[rr]) {
+                    float u = __fsub_rn((float)cs[k * RP_ROWS + rr], zrow[rr]);
+                    float ndq = __fmul_rn(snew[rr], u);
+                    int64_t off = (int64_t)rr * n + c0 + k;
+                    E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
+                    WQ[off] = ndq;
+                }
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- coordinate descent over the selected sub-blocks (src/engine.rs:600-658)
+    if (rp.do_cd && !rp.final_refit) {
+        const int n_sel = ci.st->n_sel;
+        uint8_t* cs = smem_raw;                                                      // [sbw][64]
+        float* gt = reinterpret_cast<float*>(smem_raw + al16((size_t)sbw * RP_ROWS));  // [sbw][68] gradient
+        float* wqs = gt + (size_t)sbw * RP_LD;                                       // [sbw][68] W_hat
+        for (int si = 0; si < n_sel; si++) {
+            const int s = ci.sel[si];
+            const int c0 = s * sbw, wd = min(sbw, n - c0);
+            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+                int rr = idx / wd, k = idx - rr * wd;
+                int64_t off = (int64_t)rr * n + c0 + k;
+                cs[k * RP_ROWS + rr] = CODES[off];
+                wqs[k * RP_LD + rr] = WQ[off];
+            }
+            for (int t0 = 0; t0 < wd; t0 += 128) {
+                int wt = min(128, wd - t0);
+                AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
+                gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, gt + (size_t)t0 * RP_LD, stage);
+            }
+            if (tid < rs) {
+                const int r = tid;
+                for (int sw = 0; sw < rp.cd_sweeps; sw++) {
+                    bool changed = false;
+                    int cur_gi = -1;
+                    float sc = 1.0f, z = 0.0f, maxq = 1.0f;
+                    for (int jj = 0; jj < wd; jj++) {
+                        const int j = c0 + jj;
+                        const int gi = j / g;
+                        if (gi != cur_gi) {
+                            cur_gi = gi;
+                            maxq = (float)((1u << ci.gbits[gi]) - 1u);
+                            sc = SC[(int64_t)r * ng + gi];
+                            z = ZR[(int64_t)r * ng + gi];
+                        }
+                        const float* hrow = H + (int64_t)j * n + c0;
+                        const float hjj = __ldg(hrow + jj);
+                        const float cur = wqs[jj * RP_LD + r];
+                        const float gj = gt[jj * RP_LD + r];
+                        const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
+                        float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
+                        if (q < 0.0f) q = 0.0f;
+                        if (q > maxq) q = maxq;
+                        const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
+                        const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
+                        if (qc != cs[jj * RP_ROWS + r]) {
+                            const float de = __fsub_rn(cur, newdq);
+                            float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
+                            float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
+                            my_delta = __dadd_rn(my_delta, (double)__fadd_rn(t1, t2));
+                            for (int kk = 0; kk < wd; kk++) {
+                                float* gp = &gt[kk * RP_LD + r];
+                                *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
+                            }
+                            wqs[jj * RP_LD + r] = newdq;
+                            cs[jj * RP_ROWS + r] = qc;
+                            float* ep = &E[(int64_t)r * n + j];
+                            *ep = __fadd_rn(*ep, de);
+                            my_upd++;
+                            changed = true;
+                        }
+                    }
+                    if (!changed) break;
+                }
+            }
+            __syncthreads();
+            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+                int rr = idx / wd, k = idx - rr * wd;
+                int64_t off = (int64_t)rr * n + c0 + k;
+                CODES[off] = cs[k * RP_ROWS + rr];
+                WQ[off] = wqs[k * RP_LD + rr];
+            }
+            __syncthreads();
+        }
+    }
+
+    // ---- slice reduction, rows in order
+    __syncthreads();
+    if (tid < RP_ROWS) {
+        rowdelta[tid] = (tid < rs) ? my_delta : 0.0;
+        upd_s[tid] = (tid < rs) ? my_upd : 0ull;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double d = 0.0;
+        unsigned long long u = 0ull;
+        for (int r = 0; r < rs; r++) {
+            d = __dadd_rn(d, rowdelta[r]);
+            u += upd_s[r];
+        }
+        acc_out[blockIdx.x].delta = d;
+        acc_out[blockIdx.x].updates = u;
+    }
+}
+
+int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev, int nslices, SliceAcc* acc_dev,
+                       const RepairParams& rp, int g, int sbw, cudaStream_t st) {
+    if (nslices == 0) return 0;
+    size_t smem = repair_smem_bytes(g, sbw);
+    cudaError_t e = cudaFuncSetAttribute(repair_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "repair smem attribute");
+    CDCLQ_LAUNCH(repair_pass_kernel, nslices, 256, smem, st, chunks_dev, slices_dev, acc_dev, rp);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_pass_kernel launch");
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Per-chunk end of a pass: add the slices' deltas in order, then the reference's stop rule
+// `pass_updates == 0 || gain < tol * (loss_gptq + loss_delta)` (src/engine.rs:660-665).  For the final refit
+// only the bookkeeping is updated (src/engine.rs:668-670).
+__global__ void pass_end_kernel(const ChunkInfo* __restrict__ chunks, int nchunks, const int* __restrict__ slice_begin,
+                                const SliceAcc* __restrict__ acc, RepairParams rp) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= nchunks) return;
+    ChunkState* st = chunks[c].st;
+    if (!rp.final_refit && st->done) return;
+    if (rp.final_refit && !(rp.method_cdcl && rp.do_refit)) return;
+    double d = 0.0;
+    unsigned long long u = 0ull;
+    for (int s = slice_begin[c]; s < slice_begin[c + 1]; s++) {
+        d = __dadd_rn(d, acc[s].delta);
+        u += acc[s].updates;
+    }
+    st->loss_delta = __dadd_rn(st->loss_delta, d);
+    st->updates += u;
+    if (rp.final_refit) return;
+    st->passes += 1;
+    double gain = __dsub_rn(st->prev_delta, st->loss_delta);
+    st->prev_delta = st->loss_delta;
+    if (u == 0ull || gain < rp.tol * __dadd_rn(st->loss_gptq, st->loss_delta)) st->done = 1;
+}
+
+int launch_pass_end(const ChunkInfo* chunks_dev, int nchunks, const int* slice_begin_dev, const SliceAcc* acc_dev,
+                    const RepairParams& rp, cudaStream_t st) {
+    if (nchunks == 0) return 0;
+    int threads = 128, blocks = (nchunks + threads - 1) / threads;
+    CDCLQ_LAUNCH(pass_end_kernel, blocks, threads, 0, st, chunks_dev, nchunks, slice_begin_dev, acc_dev, rp);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "pass_end_kernel launch");
+}
+
+}  // namespace cdclq

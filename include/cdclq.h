@@ -1,0 +1,225 @@
+/*
+ * cdclq.h - C ABI of the B200 (sm_100a) CDCL-GPTQ per-layer quantization path.
+ *
+ * The reference (tailot/CDCL-GPTQ, a Rust crate) has no C ABI: its drop-in unit is the Rust function
+ *     engine::quantize_layer(w, d_out, d_in, h, m, hkey, cfg, cache) -> Result<(QLayer, LayerStats)>
+ * (src/engine.rs:690-699), built on linalg.rs (Cholesky, triangular inverse, U factor, Gram accumulation)
+ * and quant.rs (grid, code).  Every entry point below replaces one of those functions; the comment on each
+ * cites the reference function it stands in for.  A Rust caller binds them with `extern "C"` (see
+ * INTEGRATION.md); Python binds them with ctypes (cdcl-gptq_b200/cdclq/_lib.py).
+ *
+ * Conventions shared by all entry points
+ *  - Plain pointers and sizes only.  Matrices are row-major.  Functions without a `_device` suffix take HOST
+ *    pointers and do their own host<->device copies; `_device` functions take device pointers and a CUDA
+ *    stream (passed as `void*`, NULL = the legacy default stream).
+ *  - Return value: CDCLQ_OK (0) or a negative CDCLQ_ERR_* status.  cdclq_last_error() then returns the
+ *    message of the last failure on the calling thread; configuration and factorisation messages keep the
+ *    reference's wording (src/engine.rs:242-255, src/linalg.rs:216-218).
+ *  - All quantized outputs are in the PERMUTED column order, exactly as `QLayer` (src/quant.rs:153-175).
+ *  - Calls are synchronous from the caller's view.  The library is not re-entrant on one prep cache.
+ */
+#ifndef CDCLQ_H_
+#define CDCLQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CDCLQ_OK 0
+#define CDCLQ_ERR_CONFIG (-1)    /* engine::validate rejected the configuration (src/engine.rs:240-258) */
+#define CDCLQ_ERR_NOT_PD (-2)    /* non-positive / non-finite Cholesky pivot (src/linalg.rs:215-219) */
+#define CDCLQ_ERR_ARG (-3)       /* null pointer or size mismatch (the reference asserts: src/engine.rs:701-702) */
+#define CDCLQ_ERR_CUDA (-4)      /* CUDA runtime failure, or no usable device */
+#define CDCLQ_ERR_NONFINITE (-5) /* non-finite Hessian entry (src/io.rs:205-212) */
+
+#define CDCLQ_METHOD_GPTQ 0 /* engine::Method::Gptq (src/engine.rs:85) */
+#define CDCLQ_METHOD_CDCL 1 /* engine::Method::Cdcl (src/engine.rs:87) */
+
+/* Mirrors engine::Config (src/engine.rs:93-144) field by field.  `threads` is the CLI's global --threads
+ * (src/main.rs:22); it only matters when row_chunk == 0, where the reference derives the row chunk from the
+ * worker count (src/engine.rs:768-770).  threads == 0 means "number of host CPUs", like rayon's default. */
+typedef struct cdclq_config {
+    uint64_t group;     /* 0 = one group per row */
+    uint64_t block;     /* lazy-update block of the GPTQ pass */
+    uint64_t sub_block; /* repair sub-block width */
+    uint64_t cd_sweeps;
+    uint64_t passes;
+    uint64_t row_chunk; /* 0 = automatic */
+    uint64_t threads;
+    double damp;
+    double skeleton_pct;
+    double refine_frac;
+    double tol;
+    uint32_t bits;
+    uint32_t skeleton_bits;
+    int32_t act_order;
+    int32_t mse_grid;
+    int32_t method; /* CDCLQ_METHOD_* */
+    int32_t refit_scales;
+} cdclq_config;
+
+/* Mirrors engine::LayerStats (src/engine.rs:173-199).  `passes_max` is an addition: the largest number of
+ * repair passes any row chunk of the layer executed (the reference does not report it). */
+typedef struct cdclq_layer_stats {
+    double loss_gptq;
+    double loss_final;
+    uint64_t subblocks_total;
+    uint64_t subblocks_refined;
+    uint64_t code_updates;
+    uint64_t skeleton_groups;
+    double bits_codes;
+    double bits_total;
+    double secs_prepare;
+    double secs_quant;
+    uint64_t passes_max;
+} cdclq_layer_stats;
+
+/* Opaque single-entry memo of the prepared factors, replacing engine::PrepCache (src/engine.rs:207-223):
+ * keyed by (hessian key, permutation); owns the device copies of U, the damped permuted Hessian and perm. */
+typedef struct cdclq_prep_cache cdclq_prep_cache;
+
+/* ---- configuration helpers ------------------------------------------------------------------------- */
+
+/* Config::default (src/engine.rs:146-167). */
+void cdclq_config_default(cdclq_config* cfg);
+/* effective_group (src/engine.rs:227-233). */
+size_t cdclq_effective_group(const cdclq_config* cfg, size_t n);
+/* ceil(n / effective_group): the `ng` of src/engine.rs:705, i.e. the length of gbits and of one row of
+ * scales/zeros. */
+size_t cdclq_num_groups(const cdclq_config* cfg, size_t n);
+/* validate (src/engine.rs:240-258).  CDCLQ_ERR_CONFIG with the reference's message on failure. */
+int cdclq_validate(const cdclq_config* cfg, size_t n);
+/* Message of the last failed call on this thread ("" if none). */
+const char* cdclq_last_error(void);
+
+/* ---- per-layer engine ------------------------------------------------------------------------------ */
+
+cdclq_prep_cache* cdclq_prep_cache_new(void);
+void cdclq_prep_cache_free(cdclq_prep_cache* cache);
+
+/* engine::quantize_layer (src/engine.rs:690-799).  Host buffers:
+ *   w      d_out x d_in f32, original column order
+ *   h      d_in x d_in f32 calibration Hessian (any positive scale)
+ *   m      optional d_in x d_in cross-covariance (NULL = symmetric calibration)
+ *   hkey   Hessian identity for the prep cache (NUL-terminated; may be NULL when cache is NULL)
+ *   cache  may be NULL (no reuse)
+ * Outputs (caller-allocated, permuted order):
+ *   perm_out d_in, gbits_out ng, codes_out d_out*d_in, scales_out / zeros_out d_out*ng, stats_out 1. */
+int cdclq_quantize_layer(const float* w, size_t d_out, size_t d_in, const float* h, const float* m,
+                         const char* hkey, const cdclq_config* cfg, cdclq_prep_cache* cache,
+                         uint32_t* perm_out, uint8_t* gbits_out, uint8_t* codes_out, float* scales_out,
+                         float* zeros_out, cdclq_layer_stats* stats_out);
+
+/* Same as cdclq_quantize_layer, plus the number of repair passes each row chunk executed
+ * (chunk_passes_out: ceil(d_out / row_chunk) entries, may be NULL). */
+int cdclq_quantize_layer_ex(const float* w, size_t d_out, size_t d_in, const float* h, const float* m,
+                            const char* hkey, const cdclq_config* cfg, cdclq_prep_cache* cache,
+                            uint32_t* perm_out, uint8_t* gbits_out, uint8_t* codes_out, float* scales_out,
+                            float* zeros_out, cdclq_layer_stats* stats_out, uint32_t* chunk_passes_out);
+
+/* Row chunk actually used for a layer with d_out rows (src/engine.rs:768-770). */
+size_t cdclq_row_chunk(const cdclq_config* cfg, size_t d_out);
+
+/* ---- model-level batch (pipeline::quantize_model's per-layer loop, src/pipeline.rs:121-175) ----------- */
+
+/* One distinct layer input (a Hessian owner in pipeline terms).  All layers pointing at the same
+ * `input` share one factorisation when their permutations agree, like the PrepCache hits the reference gets
+ * from its owner-sorted job order (src/pipeline.rs:109-112). */
+typedef struct cdclq_batch_input {
+    const float* h; /* n x n f32 */
+    size_t n;
+} cdclq_batch_input;
+
+typedef struct cdclq_batch_layer {
+    const float* w; /* d_out x n f32, original order */
+    size_t d_out;
+    size_t input; /* index into the inputs array */
+    /* outputs (permuted order), caller-allocated */
+    uint32_t* perm;   /* n */
+    uint8_t* gbits;   /* ng */
+    uint8_t* codes;   /* d_out * n */
+    float* scales;    /* d_out * ng */
+    float* zeros;     /* d_out * ng */
+    cdclq_layer_stats* stats;
+} cdclq_batch_layer;
+
+/* Quantize many layers in one batched pass: every layer's rows are in flight at once, so small layers
+ * (k/v projections) no longer leave the GPU idle.  Results are identical to calling
+ * cdclq_quantize_layer on each layer.  `on_device` = 0: all pointers are host pointers (copies inside);
+ * 1: all are device pointers (stats stays a host pointer), `stream` is used for all work. */
+int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
+                         size_t n_layers, const cdclq_config* cfg, int on_device, void* stream);
+
+/* ---- linear-algebra kernels (linalg.rs) ------------------------------------------------------------ */
+
+/* cholesky_lower (src/linalg.rs:200-276): in place on a host n x n f64 matrix; lower triangle = L. */
+int cdclq_cholesky_lower(double* a, size_t n);
+/* tri_inverse_lower (src/linalg.rs:284-347): y = L^-1 (reads the lower triangle of l only). */
+int cdclq_tri_inverse_lower(const double* l, size_t n, double* y);
+/* upper_chol_of_inverse (src/linalg.rs:362-375): U upper, H^-1 = U^T U, stored as f32. */
+int cdclq_upper_chol_of_inverse(const double* h, size_t n, float* u_out);
+/* gram_accumulate (src/linalg.rs:388-418): h (n x n f64) += x^T y over t tokens (x, y: t x n f32). */
+int cdclq_gram_accumulate(const float* x, const float* y, size_t t, size_t n, double* h);
+/* Device variant of gram_accumulate for bf16 activations on the tcgen05 tensor cores: h (f64, device)
+ * += x^T x over t tokens of x (t x n bf16, device), token chunks of 2048 accumulated in f32 then widened,
+ * as src/linalg.rs:392-416 does.  Only the lower triangle of h is written when lower_only != 0. */
+int cdclq_gram_accumulate_bf16_device(const void* x_bf16, size_t t, size_t n, double* h, int lower_only,
+                                      void* stream);
+/* Device variant of gram_accumulate for f32 activations (bit-exact with the f32 path above). */
+int cdclq_gram_accumulate_device(const float* x, const float* y, size_t t, size_t n, double* h, void* stream);
+
+/* proxy_loss (src/engine.rs:808-815): sum_r e_r (E H)_r with E = w_t - w_hat. */
+int cdclq_proxy_loss(const float* w_t, const float* w_hat, size_t rows, size_t n, const float* h,
+                     double* out);
+/* rtn_layer (src/engine.rs:822-838): round-to-nearest dequantized weights. */
+int cdclq_rtn_layer(const float* w, size_t d_out, size_t n, const cdclq_config* cfg, float* out);
+/* find_params (src/quant.rs:40-83) over `rows` independent groups of `len` values each. */
+int cdclq_find_params(const float* vals, size_t rows, size_t len, uint32_t bits, int mse, float* scales,
+                      float* zeros);
+
+/* ---- packed format (quant.rs / io.rs) -------------------------------------------------------------- */
+
+/* row_bytes (src/quant.rs:102-104). */
+size_t cdclq_row_bytes(size_t n, size_t g, const uint8_t* gbits);
+/* QLayer::pack (src/quant.rs:207-214) on the GPU: LSB-first mixed-width bit stream, d_out x row_bytes. */
+int cdclq_pack(const uint8_t* codes, size_t d_out, size_t n, size_t g, const uint8_t* gbits, uint8_t* out);
+/* QLayer::from_packed + dequantize (src/quant.rs:189-235) on the GPU: original column order, f32. */
+int cdclq_unpack_dequant(const uint8_t* packed, size_t d_out, size_t n, size_t g, const uint8_t* gbits,
+                         const uint32_t* perm, const float* scales, const float* zeros, float* out);
+
+/* ---- runtime ---------------------------------------------------------------------------------------- */
+
+/* Device-side profile of the last quantize call made on this thread: elapsed times between CUDA events
+ * recorded on the call's stream at the phase boundaries, and the algorithmic work of each phase
+ * (flops as 2 per multiply-add; repair counts only the passes each row chunk actually executed). */
+typedef struct cdclq_run_profile {
+    double ms_prepare;      /* permutations, factorisations, permuted weights */
+    double ms_phase1;       /* blocked GPTQ: one launch over all rows */
+    double ms_stats;        /* per-chunk conflict statistics: one launch */
+    double ms_repair;       /* all repair pass launches and their pass-end reductions */
+    double ms_final;        /* final scale refit */
+    double flops_phase1;    /* f32: lazy GEMMs + in-block rank-1 updates */
+    double flops_repair;    /* f32: refit and coordinate-descent gradient GEMMs of executed passes */
+    double flops_final;     /* f32: final refit GEMMs */
+    double flops_factor;    /* f64: n^3/3 Cholesky + n^3/3 triangular inverse per factorisation */
+    uint64_t repair_launches;
+    uint64_t factorisations;
+    uint64_t weights;
+    uint64_t launches;      /* kernel launches issued by the call */
+} cdclq_run_profile;
+
+int cdclq_last_run_profile(cdclq_run_profile* out);
+
+/* Number of CUDA kernel launches this library has issued so far in this process. */
+uint64_t cdclq_launch_count(void);
+/* Library version string. */
+const char* cdclq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CDCLQ_H_ */
