@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "cdclq", "libcdclq_cuda.so")
-SOURCES = ["engine.cu", "prep.cu", "gptq.cu", "repair.cu", "gemm.cu", "pack.cu", "syrk.cu"]
+SOURCES = ["engine.cu", "prep.cu", "gptq.cu", "repair.cu", "gemm.cu", "pack.cu", "syrk.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "gemm_core.cuh", "kernels.h"]
 
 

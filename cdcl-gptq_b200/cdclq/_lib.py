@@ -39,6 +39,7 @@ SIGNATURES = {
     "cdclq_gram_accumulate": (I32, [P, P, SZ, SZ, P]),
     "cdclq_gram_accumulate_bf16_device": (I32, [P, SZ, SZ, P, I32, P]),
     "cdclq_gram_accumulate_device": (I32, [P, P, SZ, SZ, P, P]),
+    "cdclq_gram_accumulate_device_noalloc": (I32, [P, P, SZ, SZ, P, P]),
     "cdclq_proxy_loss": (I32, [P, P, SZ, SZ, P, P]),
     "cdclq_rtn_layer": (I32, [P, SZ, SZ, CFG, P]),
     "cdclq_find_params": (I32, [P, SZ, SZ, ctypes.c_uint32, I32, P, P]),

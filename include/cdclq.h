@@ -170,6 +170,18 @@ int cdclq_gram_accumulate_bf16_device(const void* x_bf16, size_t t, size_t n, do
                                       void* stream);
 /* Device variant of gram_accumulate for f32 activations (bit-exact with the f32 path above). */
 int cdclq_gram_accumulate_device(const float* x, const float* y, size_t t, size_t n, double* h, void* stream);
+/* No counterpart in the reference.  Same computation and result as cdclq_gram_accumulate_device, but the
+ * library allocates no device memory for it: the per-chunk f32 scratch is a fixed array inside the library
+ * (CDCLQ_NOALLOC_GRAM_MAX_N^2 floats = 4 MiB, held on every GPU that loads the library until the process
+ * exits).  For callers that cannot call cudaMalloc where they accumulate a Hessian - a hook inside a
+ * framework whose allocator owns the device memory, or a runtime that forbids allocation after start-up.
+ * The caller passes device pointers for x, y and h.  n above CDCLQ_NOALLOC_GRAM_MAX_N returns CDCLQ_ERR_ARG.
+ * The first call on each device looks up the scratch's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls share the one scratch: calls that overlap on the GPU
+ * (other streams, other host threads) race and must be serialised by the caller. */
+#define CDCLQ_NOALLOC_GRAM_MAX_N 1024
+int cdclq_gram_accumulate_device_noalloc(const float* x, const float* y, size_t t, size_t n, double* h,
+                                         void* stream);
 
 /* proxy_loss (src/engine.rs:808-815): sum_r e_r (E H)_r with E = w_t - w_hat. */
 int cdclq_proxy_loss(const float* w_t, const float* w_hat, size_t rows, size_t n, const float* h,
