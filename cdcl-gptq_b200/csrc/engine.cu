@@ -703,7 +703,25 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     if ((rc = launch_chunk_stats(chunks_dev, (int)total_chunks, rp, st))) return rc;
     pev.record(3, st);
     uint64_t repair_launches = 0;
-    if (cdcl && (rp.do_cd || rp.do_refit)) {
+    rp.max_passes = (int)std::max<size_t>(cfg.passes, 1);
+    int sms = 148;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    // Many row chunks: one persistent launch, chunks scheduled heaviest first.  Few row chunks: one launch per
+    // pass over 64-row slices, so a chunk's rows spread over several SMs.  Both give identical results.
+    const bool persistent = total_chunks >= (size_t)(2 * sms);
+    if (cdcl && (rp.do_cd || rp.do_refit) && persistent) {
+        int* counter = nullptr;
+        if ((rc = ar.alloc(&counter, 1))) return rc;
+        if ((rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
+                                           (int)std::min<size_t>(cfg.sub_block, maxn), counter, st)))
+            return rc;
+        repair_launches = 1;
+        pev.record(4, st);
+    } else if (cdcl && (rp.do_cd || rp.do_refit)) {
         size_t max_passes = std::max<size_t>(cfg.passes, 1);
         for (size_t p = 0; p < max_passes; p++) {
             if ((rc = launch_repair_pass(chunks_dev, slices_dev, (int)slices.size(), acc_dev, rp, (int)plans[0].g,
@@ -722,7 +740,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             if ((rc = launch_pass_end(chunks_dev, (int)total_chunks, sb_dev, acc_dev, fr, st))) return rc;
         }
     }
-    if (!(cdcl && (rp.do_cd || rp.do_refit))) pev.record(4, st);
+    if (!(cdcl && (rp.do_cd || rp.do_refit)) || persistent) pev.record(4, st);
     pev.record(5, st);
     std::vector<ChunkState> states(total_chunks);
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(states.data(), states_dev, sizeof(ChunkState) * total_chunks, cudaMemcpyDeviceToHost, st));

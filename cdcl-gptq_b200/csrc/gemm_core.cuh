@@ -81,9 +81,10 @@ struct AGlobal {
     int rows_valid;
     int K;
     bool vec;  // 16-byte aligned rows and K % 4 == 0
-    // Each thread fetches 4 consecutive k of one row: thread t -> row t/4, k-quad t%4.
+    // Each thread fetches 4 consecutive k of one row: thread t -> row t%64, k-quad t/64.  A warp then covers
+    // 32 consecutive rows, which makes the transposed shared-memory stores below conflict-free.
     __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[4]) const {
-        int row = tid >> 2, q = tid & 3;
+        int row = tid & 63, q = tid >> 6;
         int k = k0 + q * 4;
         if (row < rows_valid) {
             const float* p = a + (int64_t)row * lda + k;
@@ -100,7 +101,7 @@ struct AGlobal {
         }
     }
     __device__ __forceinline__ void store(float* As, int tid, const float (&r)[4]) const {
-        int row = tid >> 2, q = tid & 3;
+        int row = tid & 63, q = tid >> 6;
 #pragma unroll
         for (int i = 0; i < 4; i++) As[(q * 4 + i) * GEMM_ALD + row] = r[i];
     }
@@ -139,11 +140,21 @@ struct BGlobal {
             for (int i = 0; i < PER; i++) r[i] = 0.0f;
         }
     }
+    // Vector stores: a warp writes 32 x PER consecutive floats of one or two k rows (no bank conflicts).
     __device__ __forceinline__ void store(float* Bs, int tid, const float (&r)[PER > 0 ? PER : 1]) const {
         constexpr int TPR = WT / PER;
         int kr = tid / TPR, c = (tid % TPR) * PER;
+        float* dst = Bs + kr * WT + c;
+        if constexpr (PER % 4 == 0) {
 #pragma unroll
-        for (int i = 0; i < PER; i++) Bs[kr * WT + c + i] = r[i];
+            for (int v = 0; v < PER / 4; v++)
+                reinterpret_cast<float4*>(dst)[v] = make_float4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+        } else if constexpr (PER == 2) {
+            *reinterpret_cast<float2*>(dst) = make_float2(r[0], r[1]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < PER; i++) dst[i] = r[i];
+        }
     }
 };
 
@@ -152,14 +163,14 @@ struct BGlobal {
 template <int TN>
 __device__ void gemm_global_a(float (&acc)[4][TN], const AGlobal& A, const BGlobal<TN>& B, int K, float* stage) {
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    float* As[2] = {stage, stage + GEMM_KT * GEMM_ALD};
-    float* Bs[2] = {stage + 2 * GEMM_KT * GEMM_ALD, stage + 2 * GEMM_KT * GEMM_ALD + GEMM_KT * 16 * TN};
+    float* const As0 = stage;                            // As[buf] = As0 + buf * KT*ALD
+    float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;
     float ra[4], rb[PER];
     A.fetch(0, tid, ra);
     B.fetch(0, tid, rb);
-    A.store(As[0], tid, ra);
-    B.store(Bs[0], tid, rb);
+    A.store(As0, tid, ra);
+    B.store(Bs0, tid, rb);
     __syncthreads();
     int buf = 0;
     for (int k0 = 0; k0 < K; k0 += GEMM_KT) {
@@ -168,10 +179,10 @@ __device__ void gemm_global_a(float (&acc)[4][TN], const AGlobal& A, const BGlob
             A.fetch(k0 + GEMM_KT, tid, ra);
             B.fetch(k0 + GEMM_KT, tid, rb);
         }
-        gemm_stage_mac<TN>(acc, As[buf], Bs[buf], ty, tx);
+        gemm_stage_mac<TN>(acc, As0 + buf * GEMM_KT * GEMM_ALD, Bs0 + buf * GEMM_KT * 16 * TN, ty, tx);
         if (more) {
-            A.store(As[buf ^ 1], tid, ra);
-            B.store(Bs[buf ^ 1], tid, rb);
+            A.store(As0 + (buf ^ 1) * GEMM_KT * GEMM_ALD, tid, ra);
+            B.store(Bs0 + (buf ^ 1) * GEMM_KT * 16 * TN, tid, rb);
         }
         __syncthreads();
         buf ^= 1;
@@ -184,11 +195,11 @@ __device__ void gemm_global_a(float (&acc)[4][TN], const AGlobal& A, const BGlob
 template <int TN>
 __device__ void gemm_smem_a(float (&acc)[4][TN], const float* As_full, const BGlobal<TN>& B, int K, float* stage) {
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    float* Bs[2] = {stage + 2 * GEMM_KT * GEMM_ALD, stage + 2 * GEMM_KT * GEMM_ALD + GEMM_KT * 16 * TN};
+    float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;
     float rb[PER];
     B.fetch(0, tid, rb);
-    B.store(Bs[0], tid, rb);
+    B.store(Bs0, tid, rb);
     __syncthreads();
     int buf = 0;
     for (int k0 = 0; k0 < K; k0 += GEMM_KT) {
@@ -196,7 +207,7 @@ __device__ void gemm_smem_a(float (&acc)[4][TN], const float* As_full, const BGl
         if (more) B.fetch(k0 + GEMM_KT, tid, rb);
         int kn = K - k0 < GEMM_KT ? K - k0 : GEMM_KT;
         const float* As = As_full + (int64_t)k0 * GEMM_ALD;
-        const float* Bb = Bs[buf];
+        const float* Bb = Bs0 + buf * GEMM_KT * 16 * TN;
         if (kn == GEMM_KT) {
             gemm_stage_mac<TN>(acc, As, Bb, ty, tx);
         } else {
@@ -210,7 +221,7 @@ __device__ void gemm_smem_a(float (&acc)[4][TN], const float* As_full, const BGl
                         acc[i][j] = __fmaf_rn(av[i], Bb[kk * (16 * TN) + ColMap<TN>::col(tx, j)], acc[i][j]);
             }
         }
-        if (more) B.store(Bs[buf ^ 1], tid, rb);
+        if (more) B.store(Bs0 + (buf ^ 1) * GEMM_KT * 16 * TN, tid, rb);
         __syncthreads();
         buf ^= 1;
     }
@@ -253,14 +264,14 @@ struct AGlobalT {
 template <int TN, class AL>
 __device__ void gemm_loader_a(float (&acc)[4][TN], const AL& A, const BGlobal<TN>& B, int K, float* stage) {
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    float* As[2] = {stage, stage + GEMM_KT * GEMM_ALD};
-    float* Bs[2] = {stage + 2 * GEMM_KT * GEMM_ALD, stage + 2 * GEMM_KT * GEMM_ALD + GEMM_KT * 16 * TN};
+    float* const As0 = stage;                            // As[buf] = As0 + buf * KT*ALD
+    float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;
     float ra[4], rb[PER];
     A.fetch(0, tid, ra);
     B.fetch(0, tid, rb);
-    A.store(As[0], tid, ra);
-    B.store(Bs[0], tid, rb);
+    A.store(As0, tid, ra);
+    B.store(Bs0, tid, rb);
     __syncthreads();
     int buf = 0;
     for (int k0 = 0; k0 < K; k0 += GEMM_KT) {
@@ -269,10 +280,10 @@ __device__ void gemm_loader_a(float (&acc)[4][TN], const AL& A, const BGlobal<TN
             A.fetch(k0 + GEMM_KT, tid, ra);
             B.fetch(k0 + GEMM_KT, tid, rb);
         }
-        gemm_stage_mac<TN>(acc, As[buf], Bs[buf], ty, tx);
+        gemm_stage_mac<TN>(acc, As0 + buf * GEMM_KT * GEMM_ALD, Bs0 + buf * GEMM_KT * 16 * TN, ty, tx);
         if (more) {
-            A.store(As[buf ^ 1], tid, ra);
-            B.store(Bs[buf ^ 1], tid, rb);
+            A.store(As0 + (buf ^ 1) * GEMM_KT * GEMM_ALD, tid, ra);
+            B.store(Bs0 + (buf ^ 1) * GEMM_KT * 16 * TN, tid, rb);
         }
         __syncthreads();
         buf ^= 1;

@@ -18,7 +18,9 @@
 namespace cdclq {
 
 constexpr int P1_ROWS = 64;
-constexpr int P1_W1LD = 65;  // w1 stride (conflict-free transposed staging)
+// w1 stride: 72 = 8 (mod 32), so the 4 columns x 8 rows a warp touches in one column step fall in 32
+// distinct banks
+constexpr int P1_W1LD = 72;
 constexpr int P1_ELD = GEMM_ALD;  // err1 stride (16-byte aligned k-major A operand)
 
 static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
@@ -29,7 +31,7 @@ size_t phase1_smem_bytes(int block) {
            (size_t)gemm_stage_floats<8>() * 4;
 }
 
-__global__ void __launch_bounds__(256, 1) gptq_phase1_kernel(const P1Item* __restrict__ items, int B, int mse) {
+__global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __restrict__ items, int B, int mse) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const P1Item it = items[blockIdx.x];
     const int n = it.n, g = it.g, ng = it.ng, rows = it.rows;

@@ -110,6 +110,7 @@ struct RepairParams {
     int cd_sweeps;
     int method_cdcl;
     int final_refit;  // 1: this launch is the final refit (runs on every chunk)
+    int max_passes;   // max(passes, 1) (src/engine.rs:595)
     double tol;
 };
 
@@ -119,6 +120,9 @@ int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev,
 int launch_pass_end(const ChunkInfo* chunks_dev, int nchunks, const int* slice_begin_dev, const SliceAcc* acc_dev,
                     const RepairParams& rp, cudaStream_t st);
 size_t repair_smem_bytes(int g, int sbw);
+// All passes + final refit of every chunk in one launch (chunks taken from *counter_dev, in array order).
+int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                             int* counter_dev, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------------------
 // Generic f32 GEMM with the fixed order: C = alpha*A*B (+ beta*C), A row-major or transposed (gemm.cu)

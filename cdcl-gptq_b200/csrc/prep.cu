@@ -183,58 +183,102 @@ __global__ void __launch_bounds__(256) chol_panel_kernel(const CholArgs* __restr
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// f64 GEMM tile (64 x 64 outputs, 256 threads, 4 x 4 per thread, K staged 8 at a time).  Thread (ty, tx)
-// owns rows ty*4..ty*4+3 and columns tx*4..tx*4+3.  Operands are fetched through callables so that the
-// trailing update, T = L Y and -Yii T share one core.  acc receives the products in increasing k.
-constexpr int DKT = 8;
-constexpr int DLD = 68;
+// f64 GEMM tile core: CTA tile (16*TM) x 64 outputs, 256 threads; thread (ty, tx) owns rows ty + 16*i and
+// columns tx + 16*j (strided, so shared-memory reads are broadcasts (A) or consecutive doubles (B)).  K is
+// staged 16 at a time with a register prefetch of the next stage.  Operands come through callables
+// fa(r, k) / fb(k, c) (bounds handled there); B_ALONG_K says which index of B is contiguous in memory so the
+// fetch is coalesced.  Each accumulator receives its products in increasing k (the fixed order).
+constexpr int DKT = 16;
+constexpr int DBLD = 65;  // odd strides: conflict-free transposed stores
+template <int TM>
+struct DTile {
+    static constexpr int ROWS = 16 * TM;
+    static constexpr int ALD = ROWS + 1;
+    static constexpr int APER = ROWS * DKT / 256;  // A elements fetched per thread per stage
+    static constexpr int BPER = 64 * DKT / 256;    // 4
+    static constexpr int SMEM_DOUBLES = 2 * DKT * ALD + 2 * DKT * DBLD;
+};
 
-// B_ALONG_K: the B operand is contiguous along k in memory (B(k, c) = P[c][k]); otherwise along c.
-template <bool B_ALONG_K, class FA, class FB>
-__device__ __forceinline__ void dgemm_tile(double (&acc)[4][4], FA fa, FB fb, int kbeg, int kend, double* As,
-                                           double* Bs) {
+template <int TM, bool B_ALONG_K, class FA, class FB>
+__device__ __forceinline__ void dgemm_tile(double (&acc)[TM][4], FA fa, FB fb, int kbeg, int kend, double* smem) {
+    using T = DTile<TM>;
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-    for (int k0 = kbeg; k0 < kend; k0 += DKT) {
-        // stage: 64 rows x 8 k of A and 8 k x 64 cols of B (512 each -> 2 per thread), each fetched along its
-        // contiguous memory direction
-        for (int q = tid; q < 64 * DKT; q += 256) {
-            int r = q / DKT, kk = q - r * DKT;
-            int k = k0 + kk;
-            As[kk * DLD + r] = (k < kend) ? fa(r, k) : 0.0;
-            int c, kb2;
-            if (B_ALONG_K) {
-                c = q / DKT;
-                kb2 = q - c * DKT;
-            } else {
-                c = q & 63;
-                kb2 = q >> 6;
-            }
-            int k2 = k0 + kb2;
-            Bs[kb2 * DLD + c] = (k2 < kend) ? fb(k2, c) : 0.0;
-        }
-        __syncthreads();
-        int kn = min(DKT, kend - k0);
-        for (int kk = 0; kk < kn; kk++) {
-            double2 a01 = *reinterpret_cast<const double2*>(As + kk * DLD + ty * 4);
-            double2 a23 = *reinterpret_cast<const double2*>(As + kk * DLD + ty * 4 + 2);
-            double2 b01 = *reinterpret_cast<const double2*>(Bs + kk * DLD + tx * 4);
-            double2 b23 = *reinterpret_cast<const double2*>(Bs + kk * DLD + tx * 4 + 2);
-            double av[4] = {a01.x, a01.y, a23.x, a23.y};
-            double bv[4] = {b01.x, b01.y, b23.x, b23.y};
+    // stage buffers: A at smem + buf * DKT*ALD, B after both A buffers (no pointer arrays: they would live in
+    // local memory when indexed by the runtime buffer number)
+    double* const As0 = smem;
+    double* const Bs0 = smem + 2 * DKT * T::ALD;
+    double ra[T::APER], rb[T::BPER];
+    auto fetch = [&](int k0) {
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+        for (int m = 0; m < T::APER; m++) {
+            int idx = tid + 256 * m, r = idx / DKT, k = k0 + (idx % DKT);
+            ra[m] = (k < kend) ? fa(r, k) : 0.0;
+        }
+#pragma unroll
+        for (int m = 0; m < T::BPER; m++) {
+            int idx = tid + 256 * m, c, k;
+            if (B_ALONG_K) {
+                c = idx / DKT;
+                k = k0 + (idx % DKT);
+            } else {
+                k = k0 + idx / 64;
+                c = idx % 64;
+            }
+            rb[m] = (k < kend) ? fb(k, c) : 0.0;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int m = 0; m < T::APER; m++) {
+            int idx = tid + 256 * m, r = idx / DKT, kk = idx % DKT;
+            As0[buf * DKT * T::ALD + kk * T::ALD + r] = ra[m];
+        }
+#pragma unroll
+        for (int m = 0; m < T::BPER; m++) {
+            int idx = tid + 256 * m, c, kk;
+            if (B_ALONG_K) {
+                c = idx / DKT;
+                kk = idx % DKT;
+            } else {
+                kk = idx / 64;
+                c = idx % 64;
+            }
+            Bs0[buf * DKT * DBLD + kk * DBLD + c] = rb[m];
+        }
+    };
+    if (kbeg >= kend) return;
+    fetch(kbeg);
+    store(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += DKT) {
+        const bool more = k0 + DKT < kend;
+        if (more) fetch(k0 + DKT);
+        const double* A = As0 + buf * DKT * T::ALD;
+        const double* Bq = Bs0 + buf * DKT * DBLD;
+#pragma unroll
+        for (int kk = 0; kk < DKT; kk++) {
+            double av[TM], bv[4];
+#pragma unroll
+            for (int i = 0; i < TM; i++) av[i] = A[kk * T::ALD + ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) bv[j] = Bq[kk * DBLD + tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < TM; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) acc[i][j] = __fma_rn(av[i], bv[j], acc[i][j]);
         }
+        if (more) store(buf ^ 1);
         __syncthreads();
+        buf ^= 1;
     }
 }
 
 // Cholesky step 3 (src/linalg.rs:242-271): A22[i][c] -= sum_t P[i][t] P[c][t] for kend <= c <= i < n,
 // lower 64x64 tiles only (the reference also updates some upper-triangle garbage that is never read).
+// Zero-padded k beyond kb contributes exact zeros; each accumulator runs t = 0..kb-1 in order.
 __global__ void __launch_bounds__(256) chol_trail_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
-    __shared__ __align__(16) double As[DKT * DLD];
-    __shared__ __align__(16) double Bs[DKT * DLD];
+    __shared__ __align__(16) double smem[DTile<4>::SMEM_DOUBLES];
     const CholArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
     double* A = ar.a;
@@ -259,15 +303,15 @@ __global__ void __launch_bounds__(256) chol_trail_kernel(const CholArgs* __restr
         int cc = c0 + c;
         return (cc < n) ? A[(int64_t)cc * n + k + t] : 0.0;
     };
-    dgemm_tile<true>(acc, fa, fb, 0, kb, As, Bs);
+    dgemm_tile<4, true>(acc, fa, fb, 0, kb, smem);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 #pragma unroll
     for (int a = 0; a < 4; a++) {
-        int i = r0 + ty * 4 + a;
+        int i = r0 + ty + 16 * a;
         if (i >= n) continue;
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-            int c = c0 + tx * 4 + b;
+            int c = c0 + tx + 16 * b;
             if (c <= i) {
                 double* p = A + (int64_t)i * n + c;
                 *p = __dsub_rn(*p, acc[a][b]);
@@ -339,75 +383,69 @@ __global__ void __launch_bounds__(128) tri_diag_kernel(const TriArgs* __restrict
 }
 
 // Triangular inverse step 2 (src/linalg.rs:307-325): T[i][j] = sum_k L[s+i][k] Y[k][j], k in [0, s).
-// Y is lower triangular: for the column tile starting at j0 every k < j0 multiplies an exact zero.
+// Y is lower triangular: for the column tile starting at j0 every k < j0 multiplies an exact zero, so the
+// accumulation starts at k = j0.  One CTA covers all w <= 96 rows of the block and 64 columns.
 __global__ void __launch_bounds__(256) tri_gemm1_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
-    __shared__ __align__(16) double As[DKT * DLD];
-    __shared__ __align__(16) double Bs[DKT * DLD];
-    const TriArgs ar = args[blockIdx.z];
+    __shared__ __align__(16) double smem[DTile<6>::SMEM_DOUBLES];
+    const TriArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
-    const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
-    double acc[4][4];
+    const int j0 = blockIdx.x * 64;
+    double acc[6][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 6; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
     const double* L = ar.l;
     const double* Y = ar.y;
-    auto fa = [&](int r, int k) -> double {
-        int i = i0 + r;
-        return (i < w) ? L[(int64_t)(s + i) * n + k] : 0.0;
-    };
+    auto fa = [&](int r, int k) -> double { return (r < w) ? L[(int64_t)(s + r) * n + k] : 0.0; };
     auto fb = [&](int k, int c) -> double {
         int j = j0 + c;
         return (j < s) ? Y[(int64_t)k * n + j] : 0.0;
     };
-    dgemm_tile<false>(acc, fa, fb, j0, s, As, Bs);
+    dgemm_tile<6, false>(acc, fa, fb, j0, s, smem);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 #pragma unroll
-    for (int a = 0; a < 4; a++) {
-        int i = i0 + ty * 4 + a;
+    for (int a = 0; a < 6; a++) {
+        int i = ty + 16 * a;
         if (i >= w) continue;
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-            int j = j0 + tx * 4 + b;
+            int j = j0 + tx + 16 * b;
             if (j < s) ar.t[(int64_t)i * n + j] = acc[a][b];
         }
     }
 }
 
 // Triangular inverse step 3 (src/linalg.rs:326-341): Y[s+i][j] = -sum_k Yii[i][k] T[k][j], k in [0, w);
-// Yii is lower triangular, so only k <= i contribute.
+// Yii is lower triangular, so the k > i terms are exact zeros.
 __global__ void __launch_bounds__(256) tri_gemm2_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
-    __shared__ __align__(16) double As[DKT * DLD];
-    __shared__ __align__(16) double Bs[DKT * DLD];
-    const TriArgs ar = args[blockIdx.z];
+    __shared__ __align__(16) double smem[DTile<6>::SMEM_DOUBLES];
+    const TriArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
-    const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
-    double acc[4][4];
+    const int j0 = blockIdx.x * 64;
+    double acc[6][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 6; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
     double* Y = ar.y;
     const double* T = ar.t;
     auto fa = [&](int r, int k) -> double {
-        int i = i0 + r;
-        return (i < w && k <= i) ? Y[(int64_t)(s + i) * n + (s + k)] : 0.0;
+        return (r < w && k <= r) ? Y[(int64_t)(s + r) * n + (s + k)] : 0.0;
     };
     auto fb = [&](int k, int c) -> double {
         int j = j0 + c;
         return (j < s) ? T[(int64_t)k * n + j] : 0.0;
     };
-    int kend = min(w, i0 + 64);
-    dgemm_tile<false>(acc, fa, fb, 0, kend, As, Bs);
+    dgemm_tile<6, false>(acc, fa, fb, 0, w, smem);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 #pragma unroll
-    for (int a = 0; a < 4; a++) {
-        int i = i0 + ty * 4 + a;
+    for (int a = 0; a < 6; a++) {
+        int i = ty + 16 * a;
         if (i >= w) continue;
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-            int j = j0 + tx * 4 + b;
+            int j = j0 + tx + 16 * b;
             if (j < s) Y[(int64_t)(s + i) * n + j] = -acc[a][b];
         }
     }
@@ -420,7 +458,7 @@ static int run_tri_inverse(const TriArgs* args_dev, int nitems, int n, cudaStrea
         cudaFuncSetAttribute(tri_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         CDCLQ_LAUNCH(tri_diag_kernel, nitems, 128, smem, st, args_dev, n, s, w);
         if (s > 0) {
-            dim3 g((s + 63) / 64, (w + 63) / 64, nitems);
+            dim3 g((s + 63) / 64, nitems);
             CDCLQ_LAUNCH(tri_gemm1_kernel, g, 256, 0, st, args_dev, n, s, w);
             CDCLQ_LAUNCH(tri_gemm2_kernel, g, 256, 0, st, args_dev, n, s, w);
         }

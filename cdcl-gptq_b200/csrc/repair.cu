@@ -98,14 +98,14 @@ struct ACodes {
     int rows_valid;
     int K;
     __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[4]) const {
-        int row = tid >> 2, q = tid & 3;
+        int row = tid & 63, q = tid >> 6;
         int k = k0 + q * 4;
 #pragma unroll
         for (int i = 0; i < 4; i++)
             r[i] = (row < rows_valid && k + i < K) ? __fsub_rn((float)cs[(k + i) * RP_ROWS + row], zr[row]) : 0.0f;
     }
     __device__ __forceinline__ void store(float* As, int tid, const float (&r)[4]) const {
-        int row = tid >> 2, q = tid & 3;
+        int row = tid & 63, q = tid >> 6;
 #pragma unroll
         for (int i = 0; i < 4; i++) As[(q * 4 + i) * GEMM_ALD + row] = r[i];
     }
@@ -166,18 +166,25 @@ __device__ void gemm_to_tile(const AL& A, const float* b, int64_t ldb, int64_t c
     __syncthreads();
 }
 
-// Shared-memory layout of the repair kernel: a body shared by the refit (group code tile + one 128-column
-// result tile) and the coordinate descent (sub-block code tile, gradient tile, W_hat tile), per-row scalars,
-// then the GEMM staging buffers.
+// Shared-memory layout of the repair kernels: a body shared by the refit (group code tile + one 128-column
+// result tile) and the coordinate descent (sub-block code tile, gradient tile, W_hat tile and the sub-block
+// Hessian), per-row scalars, then the GEMM staging buffers.
+constexpr int HSS_MAX_BYTES = 16384;  // sub-blocks up to 64 columns keep their whole Hessian block on chip
+
 struct RepairLayout {
     size_t body, zrow, snew, accept, rowdelta, upd, stage, total;
 };
+
+static __host__ __device__ inline size_t cd_hss_bytes(int sbw) {
+    size_t full = (size_t)sbw * sbw * 4;
+    return full <= (size_t)HSS_MAX_BYTES ? al16(full) : al16((size_t)sbw * 4);
+}
 
 static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
     RepairLayout L;
     size_t gcap = (size_t)(g < 1024 ? g : 1024);
     size_t refit = al16(gcap * RP_ROWS) + al16((size_t)128 * RP_LD * 4);
-    size_t cd = al16((size_t)sbw * RP_ROWS) + 2 * al16((size_t)sbw * RP_LD * 4);
+    size_t cd = al16((size_t)sbw * RP_ROWS) + 2 * al16((size_t)sbw * RP_LD * 4) + cd_hss_bytes(sbw);
     L.body = refit > cd ? refit : cd;
     L.zrow = L.body;
     L.snew = L.zrow + RP_ROWS * 4;
@@ -191,217 +198,374 @@ static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
 
 size_t repair_smem_bytes(int g, int sbw) { return repair_layout(g, sbw).total; }
 
-// ---------------------------------------------------------------------------------------------------------
-// One repair pass (or the final refit) over a row slice.
-__global__ void __launch_bounds__(256) repair_pass_kernel(const ChunkInfo* __restrict__ chunks,
-                                                          const SliceItem* __restrict__ slices,
-                                                          SliceAcc* __restrict__ acc_out, RepairParams rp) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const SliceItem sl = slices[blockIdx.x];
-    const ChunkInfo ci = chunks[sl.chunk];
-    const int tid = threadIdx.x;
-    if (!rp.final_refit && ci.st->done) return;  // this chunk has converged (src/engine.rs:663-665)
+struct TileSmem {
+    unsigned char* body;
+    float* zrow;
+    float* snew;
+    int* accept;
+    double* rowdelta;
+    unsigned long long* rowupd;
+    float* stage;
+};
 
-    const int n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw, rs = sl.rs;
-    const int64_t rbase = (int64_t)sl.r0 * n;   // element offset of the slice inside the chunk
-    const int64_t gbase = (int64_t)sl.r0 * ng;
-    float* E = ci.e + rbase;
-    float* WQ = ci.wq + rbase;
-    uint8_t* CODES = ci.codes + rbase;
-    float* SC = ci.scales + gbase;
-    const float* ZR = ci.zeros + gbase;
-    const float* H = ci.h;
-
-    const size_t gcap = (size_t)(g < 1024 ? g : 1024);
+__device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw) {
     const RepairLayout L = repair_layout(g, sbw);
-    float* zrow = reinterpret_cast<float*>(smem_raw + L.zrow);        // [64] zero point of the group
-    float* snew = reinterpret_cast<float*>(smem_raw + L.snew);        // [64] accepted new scale
-    int* accept = reinterpret_cast<int*>(smem_raw + L.accept);        // [64]
-    double* rowdelta = reinterpret_cast<double*>(smem_raw + L.rowdelta);
-    unsigned long long* upd_s = reinterpret_cast<unsigned long long*>(smem_raw + L.upd);
-    float* stage = reinterpret_cast<float*>(smem_raw + L.stage);
+    TileSmem t;
+    t.body = raw;
+    t.zrow = reinterpret_cast<float*>(raw + L.zrow);
+    t.snew = reinterpret_cast<float*>(raw + L.snew);
+    t.accept = reinterpret_cast<int*>(raw + L.accept);
+    t.rowdelta = reinterpret_cast<double*>(raw + L.rowdelta);
+    t.rowupd = reinterpret_cast<unsigned long long*>(raw + L.upd);
+    t.stage = reinterpret_cast<float*>(raw + L.stage);
+    return t;
+}
 
-    double my_delta = 0.0;            // thread r < rs: this row's accepted loss deltas
-    unsigned long long my_upd = 0ull;
-
-    // ---- closed-form scale refit of every (row, group), groups in order (src/engine.rs:534-589)
-    if (rp.do_refit) {
-        uint8_t* cs = smem_raw;                                              // [gcap][64] codes of the group
-        float* tile = reinterpret_cast<float*>(smem_raw + al16(gcap * RP_ROWS));  // [128][68] G, then u H_CC
-        for (int gi = 0; gi < ng; gi++) {
-            const int c0 = gi * g, wd = min(g, n - c0);
-            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-                int rr = idx / wd, k = idx - rr * wd;
-                cs[k * RP_ROWS + rr] = CODES[(int64_t)rr * n + c0 + k];
-            }
-            if (tid < RP_ROWS) zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
-            __syncthreads();
-            // num = sum_k u_k * G_k, G = E H[:, c0:c1]
-            float num = 0.0f, den = 0.0f;
-            for (int t0 = 0; t0 < wd; t0 += 128) {
-                int wt = min(128, wd - t0);
-                AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
-                gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, tile, stage);
-                if (tid < rs) {
-                    float zr = zrow[tid];
-                    for (int k = 0; k < wt; k++) {
-                        float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
-                        num = __fadd_rn(num, __fmul_rn(u, tile[k * RP_LD + tid]));
-                    }
-                }
-                __syncthreads();
-            }
-            // den = sum_k u_k * (u H_CC)_k
-            for (int t0 = 0; t0 < wd; t0 += 128) {
-                int wt = min(128, wd - t0);
-                ACodes A{cs, zrow, rs, wd};
-                gemm_to_tile(A, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0), wt, wd, tile, stage);
-                if (tid < rs) {
-                    float zr = zrow[tid];
-                    for (int k = 0; k < wt; k++) {
-                        float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
-                        den = __fadd_rn(den, __fmul_rn(u, tile[k * RP_LD + tid]));
-                    }
-                }
-                __syncthreads();
-            }
-            if (tid < RP_ROWS) accept[tid] = 0;
+// ---------------------------------------------------------------------------------------------------------
+// Closed-form scale refit of every (row, group) of the rows [r0, r0 + rs) of a chunk, groups in order
+// (src/engine.rs:534-589).  Thread r < rs accumulates its row's accepted loss deltas and refits.
+__device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& sm, double& my_delta,
+                           unsigned long long& my_upd) {
+    const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng;
+    const size_t gcap = (size_t)(g < 1024 ? g : 1024);
+    float* E = ci.e + (int64_t)r0 * n;
+    float* WQ = ci.wq + (int64_t)r0 * n;
+    const uint8_t* CODES = ci.codes + (int64_t)r0 * n;
+    float* SC = ci.scales + (int64_t)r0 * ng;
+    const float* ZR = ci.zeros + (int64_t)r0 * ng;
+    const float* H = ci.h;
+    uint8_t* cs = sm.body;                                                   // [gcap][64] codes of the group
+    float* tile = reinterpret_cast<float*>(sm.body + al16(gcap * RP_ROWS));  // [128][68] G, then u H_CC
+    for (int gi = 0; gi < ng; gi++) {
+        const int c0 = gi * g, wd = min(g, n - c0);
+        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+            int rr = idx / wd, k = idx - rr * wd;
+            cs[k * RP_ROWS + rr] = CODES[(int64_t)rr * n + c0 + k];
+        }
+        if (tid < RP_ROWS) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
+        __syncthreads();
+        // num = sum_k u_k * G_k with G = E H[:, c0:c1]
+        float num = 0.0f, den = 0.0f;
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
+            gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, tile, sm.stage);
             if (tid < rs) {
-                if (den > 1e-30f) {
-                    float s_old = SC[(int64_t)tid * ng + gi];
-                    float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
-                    if (!(s_new >= kF16MinNormal)) s_new = kF16MinNormal;  // f32::max(x, MIN)
-                    float d = __fsub_rn(s_new, s_old);
-                    float dlf = __fadd_rn(__fmul_rn(__fmul_rn(-2.0f, d), num), __fmul_rn(__fmul_rn(d, d), den));
-                    double dl = (double)dlf;
-                    if (dl < 0.0) {
-                        SC[(int64_t)tid * ng + gi] = s_new;
-                        snew[tid] = s_new;
-                        accept[tid] = 1;
-                        my_delta = __dadd_rn(my_delta, dl);
-                        my_upd++;
-                    }
-                }
-            }
-            __syncthreads();
-            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-                int rr = idx / wd, k = idx - rr * wd;
-                if (accept[rr]) {
-                    float u = __fsub_rn((float)cs[k * RP_ROWS + rr], zrow[rr]);
-                    float ndq = __fmul_rn(snew[rr], u);
-                    int64_t off = (int64_t)rr * n + c0 + k;
-                    E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
-                    WQ[off] = ndq;
+                const float zr = sm.zrow[tid];
+                for (int k = 0; k < wt; k++) {
+                    float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
+                    num = __fadd_rn(num, __fmul_rn(u, tile[k * RP_LD + tid]));
                 }
             }
             __syncthreads();
         }
-    }
-
-    // ---- coordinate descent over the selected sub-blocks (src/engine.rs:600-658)
-    if (rp.do_cd && !rp.final_refit) {
-        const int n_sel = ci.st->n_sel;
-        uint8_t* cs = smem_raw;                                                      // [sbw][64]
-        float* gt = reinterpret_cast<float*>(smem_raw + al16((size_t)sbw * RP_ROWS));  // [sbw][68] gradient
-        float* wqs = gt + (size_t)sbw * RP_LD;                                       // [sbw][68] W_hat
-        for (int si = 0; si < n_sel; si++) {
-            const int s = ci.sel[si];
-            const int c0 = s * sbw, wd = min(sbw, n - c0);
-            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-                int rr = idx / wd, k = idx - rr * wd;
-                int64_t off = (int64_t)rr * n + c0 + k;
-                cs[k * RP_ROWS + rr] = CODES[off];
-                wqs[k * RP_LD + rr] = WQ[off];
-            }
-            for (int t0 = 0; t0 < wd; t0 += 128) {
-                int wt = min(128, wd - t0);
-                AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
-                gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, gt + (size_t)t0 * RP_LD, stage);
-            }
+        // den = sum_k u_k * (u H_CC)_k
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            ACodes A{cs, sm.zrow, rs, wd};
+            gemm_to_tile(A, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0), wt, wd, tile, sm.stage);
             if (tid < rs) {
-                const int r = tid;
-                for (int sw = 0; sw < rp.cd_sweeps; sw++) {
-                    bool changed = false;
-                    int cur_gi = -1;
-                    float sc = 1.0f, z = 0.0f, maxq = 1.0f;
-                    for (int jj = 0; jj < wd; jj++) {
-                        const int j = c0 + jj;
-                        const int gi = j / g;
-                        if (gi != cur_gi) {
-                            cur_gi = gi;
-                            maxq = (float)((1u << ci.gbits[gi]) - 1u);
-                            sc = SC[(int64_t)r * ng + gi];
-                            z = ZR[(int64_t)r * ng + gi];
-                        }
-                        const float* hrow = H + (int64_t)j * n + c0;
-                        const float hjj = __ldg(hrow + jj);
-                        const float cur = wqs[jj * RP_LD + r];
-                        const float gj = gt[jj * RP_LD + r];
-                        const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
-                        float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
-                        if (q < 0.0f) q = 0.0f;
-                        if (q > maxq) q = maxq;
-                        const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
-                        const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
-                        if (qc != cs[jj * RP_ROWS + r]) {
-                            const float de = __fsub_rn(cur, newdq);
-                            float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
-                            float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
-                            my_delta = __dadd_rn(my_delta, (double)__fadd_rn(t1, t2));
+                const float zr = sm.zrow[tid];
+                for (int k = 0; k < wt; k++) {
+                    float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
+                    den = __fadd_rn(den, __fmul_rn(u, tile[k * RP_LD + tid]));
+                }
+            }
+            __syncthreads();
+        }
+        if (tid < RP_ROWS) sm.accept[tid] = 0;
+        if (tid < rs && den > 1e-30f) {
+            const float s_old = SC[(int64_t)tid * ng + gi];
+            float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
+            if (!(s_new >= kF16MinNormal)) s_new = kF16MinNormal;  // f32::max(x, MIN)
+            const float d = __fsub_rn(s_new, s_old);
+            const float dlf = __fadd_rn(__fmul_rn(__fmul_rn(-2.0f, d), num), __fmul_rn(__fmul_rn(d, d), den));
+            const double dl = (double)dlf;
+            if (dl < 0.0) {
+                SC[(int64_t)tid * ng + gi] = s_new;
+                sm.snew[tid] = s_new;
+                sm.accept[tid] = 1;
+                my_delta = __dadd_rn(my_delta, dl);
+                my_upd++;
+            }
+        }
+        __syncthreads();
+        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+            int rr = idx / wd, k = idx - rr * wd;
+            if (sm.accept[rr]) {
+                float u = __fsub_rn((float)cs[k * RP_ROWS + rr], sm.zrow[rr]);
+                float ndq = __fmul_rn(sm.snew[rr], u);
+                int64_t off = (int64_t)rr * n + c0 + k;
+                E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
+                WQ[off] = ndq;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Coordinate descent over the selected sub-blocks for rows [r0, r0 + rs) (src/engine.rs:600-658).
+__device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
+                        unsigned long long& my_upd) {
+    const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
+    float* E = ci.e + (int64_t)r0 * n;
+    float* WQ = ci.wq + (int64_t)r0 * n;
+    uint8_t* CODES = ci.codes + (int64_t)r0 * n;
+    const float* SC = ci.scales + (int64_t)r0 * ng;
+    const float* ZR = ci.zeros + (int64_t)r0 * ng;
+    const float* H = ci.h;
+    const int n_sel = ci.st->n_sel;
+    uint8_t* cs = sm.body;                                                      // [sbw][64]
+    float* gt = reinterpret_cast<float*>(sm.body + al16((size_t)sbw * RP_ROWS));  // [sbw][68] block gradient
+    float* wqs = gt + (size_t)sbw * RP_LD;                                      // [sbw][68] W_hat
+    float* hss = wqs + (size_t)sbw * RP_LD;                                     // [sbw][sbw] or its diagonal
+    const bool hss_full = (size_t)sbw * sbw * 4 <= (size_t)HSS_MAX_BYTES;
+    for (int si = 0; si < n_sel; si++) {
+        const int s = ci.sel[si];
+        const int c0 = s * sbw, wd = min(sbw, n - c0);
+        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+            int rr = idx / wd, k = idx - rr * wd;
+            int64_t off = (int64_t)rr * n + c0 + k;
+            cs[k * RP_ROWS + rr] = CODES[off];
+            wqs[k * RP_LD + rr] = WQ[off];
+        }
+        if (hss_full) {
+            for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
+                int a = idx / wd, b = idx - a * wd;
+                hss[idx] = __ldg(H + (int64_t)(c0 + a) * n + c0 + b);
+            }
+        } else {
+            for (int a = tid; a < wd; a += blockDim.x) hss[a] = __ldg(H + (int64_t)(c0 + a) * n + c0 + a);
+        }
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
+            gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, gt + (size_t)t0 * RP_LD, sm.stage);
+        }
+        if (tid < rs) {
+            const int r = tid;
+            for (int sw = 0; sw < cd_sweeps; sw++) {
+                bool changed = false;
+                int cur_gi = -1;
+                float sc = 1.0f, z = 0.0f, maxq = 1.0f;
+                for (int jj = 0; jj < wd; jj++) {
+                    const int j = c0 + jj;
+                    const int gi = j / g;
+                    if (gi != cur_gi) {
+                        cur_gi = gi;
+                        maxq = (float)((1u << ci.gbits[gi]) - 1u);
+                        sc = SC[(int64_t)r * ng + gi];
+                        z = ZR[(int64_t)r * ng + gi];
+                    }
+                    const float hjj = hss_full ? hss[jj * wd + jj] : hss[jj];
+                    const float cur = wqs[jj * RP_LD + r];
+                    const float gj = gt[jj * RP_LD + r];
+                    const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
+                    float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
+                    if (q < 0.0f) q = 0.0f;
+                    if (q > maxq) q = maxq;
+                    const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
+                    const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
+                    if (qc != cs[jj * RP_ROWS + r]) {
+                        // closed-form loss change, then the rank-1 gradient update (src/engine.rs:634-650)
+                        const float de = __fsub_rn(cur, newdq);
+                        const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
+                        const float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
+                        my_delta = __dadd_rn(my_delta, (double)__fadd_rn(t1, t2));
+                        if (hss_full) {
+                            const float* hrow = hss + jj * wd;
+                            for (int kk = 0; kk < wd; kk++) {
+                                float* gp = &gt[kk * RP_LD + r];
+                                *gp = __fadd_rn(*gp, __fmul_rn(de, hrow[kk]));
+                            }
+                        } else {
+                            const float* hrow = H + (int64_t)j * n + c0;
                             for (int kk = 0; kk < wd; kk++) {
                                 float* gp = &gt[kk * RP_LD + r];
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
                             }
-                            wqs[jj * RP_LD + r] = newdq;
-                            cs[jj * RP_ROWS + r] = qc;
-                            float* ep = &E[(int64_t)r * n + j];
-                            *ep = __fadd_rn(*ep, de);
-                            my_upd++;
-                            changed = true;
                         }
+                        wqs[jj * RP_LD + r] = newdq;
+                        cs[jj * RP_ROWS + r] = qc;
+                        float* ep = &E[(int64_t)r * n + j];
+                        *ep = __fadd_rn(*ep, de);
+                        my_upd++;
+                        changed = true;
                     }
-                    if (!changed) break;
                 }
+                if (!changed) break;
             }
-            __syncthreads();
-            for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-                int rr = idx / wd, k = idx - rr * wd;
-                int64_t off = (int64_t)rr * n + c0 + k;
-                CODES[off] = cs[k * RP_ROWS + rr];
-                WQ[off] = wqs[k * RP_LD + rr];
-            }
-            __syncthreads();
         }
+        __syncthreads();
+        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+            int rr = idx / wd, k = idx - rr * wd;
+            int64_t off = (int64_t)rr * n + c0 + k;
+            CODES[off] = cs[k * RP_ROWS + rr];
+            WQ[off] = wqs[k * RP_LD + rr];
+        }
+        __syncthreads();
     }
+}
 
-    // ---- slice reduction, rows in order
+// Sum of the tile's per-row results, rows in order; valid in thread 0.  Ends synchronised.
+__device__ __forceinline__ void tile_reduce(int rs, const TileSmem& sm, double my_delta, unsigned long long my_upd,
+                                            double& d, unsigned long long& u) {
+    const int tid = threadIdx.x;
     __syncthreads();
     if (tid < RP_ROWS) {
-        rowdelta[tid] = (tid < rs) ? my_delta : 0.0;
-        upd_s[tid] = (tid < rs) ? my_upd : 0ull;
+        sm.rowdelta[tid] = (tid < rs) ? my_delta : 0.0;
+        sm.rowupd[tid] = (tid < rs) ? my_upd : 0ull;
     }
     __syncthreads();
+    d = 0.0;
+    u = 0ull;
     if (tid == 0) {
-        double d = 0.0;
-        unsigned long long u = 0ull;
         for (int r = 0; r < rs; r++) {
-            d = __dadd_rn(d, rowdelta[r]);
-            u += upd_s[r];
+            d = __dadd_rn(d, sm.rowdelta[r]);
+            u += sm.rowupd[r];
         }
+    }
+    __syncthreads();
+}
+
+// The reference's stop rule after a pass (src/engine.rs:660-665), in thread 0 / one thread.
+__device__ __forceinline__ void apply_pass(ChunkState* st, double pass_delta, unsigned long long pass_upd, double tol) {
+    st->loss_delta = __dadd_rn(st->loss_delta, pass_delta);
+    st->updates += pass_upd;
+    st->passes += 1;
+    const double gain = __dsub_rn(st->prev_delta, st->loss_delta);
+    st->prev_delta = st->loss_delta;
+    if (pass_upd == 0ull || gain < tol * __dadd_rn(st->loss_gptq, st->loss_delta)) st->done = 1;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Mode A - one launch per pass over 64-row slices (used when there are few row chunks, so that a chunk's
+// rows spread over several SMs); pass_end_kernel then reduces each chunk's slices in order.
+__global__ void __launch_bounds__(256, 2) repair_pass_kernel(const ChunkInfo* __restrict__ chunks,
+                                                             const SliceItem* __restrict__ slices,
+                                                             SliceAcc* __restrict__ acc_out, RepairParams rp) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ ChunkInfo ci;  // chunk descriptor kept on chip (not in registers across the tile loops)
+    const SliceItem sl = slices[blockIdx.x];
+    if (threadIdx.x == 0) ci = chunks[sl.chunk];
+    __syncthreads();
+    if (!rp.final_refit && ci.st->done) return;  // this chunk has converged (src/engine.rs:663-665)
+    const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
+    double my_delta = 0.0;
+    unsigned long long my_upd = 0ull;
+    if (rp.do_refit) refit_tile(ci, sl.r0, sl.rs, sm, my_delta, my_upd);
+    if (rp.do_cd && !rp.final_refit) cd_tile(ci, sl.r0, sl.rs, rp.cd_sweeps, sm, my_delta, my_upd);
+    double d;
+    unsigned long long u;
+    tile_reduce(sl.rs, sm, my_delta, my_upd, d, u);
+    if (threadIdx.x == 0) {
         acc_out[blockIdx.x].delta = d;
         acc_out[blockIdx.x].updates = u;
     }
+}
+
+// Mode B - persistent: each CTA takes whole row chunks from a counter (heaviest first) and runs all of a
+// chunk's passes, its stop rule and its final refit itself, so no launch-wide barrier separates passes.  The
+// arithmetic and every reduction order are those of mode A (tiles of 64 rows = mode A's slices).
+__global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkInfo* __restrict__ chunks, int nchunks,
+                                                                   RepairParams rp, int* __restrict__ counter) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int s_chunk, s_done;
+    __shared__ ChunkInfo ci;  // chunk descriptor kept on chip (not in registers across the tile loops)
+    const int tid = threadIdx.x;
+    for (;;) {
+        if (tid == 0) {
+            s_chunk = atomicAdd(counter, 1);
+            if (s_chunk < nchunks) ci = chunks[s_chunk];
+        }
+        __syncthreads();
+        const int c = s_chunk;
+        if (c >= nchunks) return;
+        ChunkState* st = ci.st;
+        const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
+        if (tid == 0) s_done = st->done;
+        __syncthreads();
+        for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
+            double pd = 0.0;
+            unsigned long long pu = 0ull;
+            for (int r0 = 0; r0 < ci.rows; r0 += RP_ROWS) {
+                const int rs = min(RP_ROWS, ci.rows - r0);
+                double my_delta = 0.0;
+                unsigned long long my_upd = 0ull;
+                if (rp.do_refit) refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+                if (rp.do_cd) cd_tile(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+                double d;
+                unsigned long long u;
+                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                if (tid == 0) {
+                    pd = __dadd_rn(pd, d);
+                    pu += u;
+                }
+            }
+            if (tid == 0) {
+                apply_pass(st, pd, pu, rp.tol);
+                s_done = st->done;
+            }
+            __syncthreads();
+        }
+        if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
+            double fd = 0.0;
+            unsigned long long fu = 0ull;
+            for (int r0 = 0; r0 < ci.rows; r0 += RP_ROWS) {
+                const int rs = min(RP_ROWS, ci.rows - r0);
+                double my_delta = 0.0;
+                unsigned long long my_upd = 0ull;
+                refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+                double d;
+                unsigned long long u;
+                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                if (tid == 0) {
+                    fd = __dadd_rn(fd, d);
+                    fu += u;
+                }
+            }
+            if (tid == 0) {
+                st->loss_delta = __dadd_rn(st->loss_delta, fd);
+                st->updates += fu;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+static int set_repair_smem(const void* fn, size_t smem) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair smem attribute");
 }
 
 int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev, int nslices, SliceAcc* acc_dev,
                        const RepairParams& rp, int g, int sbw, cudaStream_t st) {
     if (nslices == 0) return 0;
     size_t smem = repair_smem_bytes(g, sbw);
-    cudaError_t e = cudaFuncSetAttribute(repair_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_error(e, "repair smem attribute");
+    int rc = set_repair_smem((const void*)repair_pass_kernel, smem);
+    if (rc) return rc;
     CDCLQ_LAUNCH(repair_pass_kernel, nslices, 256, smem, st, chunks_dev, slices_dev, acc_dev, rp);
-    e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_pass_kernel launch");
+}
+
+int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                             int* counter_dev, cudaStream_t st) {
+    if (nchunks == 0) return 0;
+    size_t smem = repair_smem_bytes(g, sbw);
+    int rc = set_repair_smem((const void*)repair_persistent_kernel, smem);
+    if (rc) return rc;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    int grid = sms * per_sm;
+    if (grid > nchunks) grid = nchunks;
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
+    CDCLQ_LAUNCH(repair_persistent_kernel, grid, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_persistent_kernel launch");
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -421,13 +585,12 @@ __global__ void pass_end_kernel(const ChunkInfo* __restrict__ chunks, int nchunk
         d = __dadd_rn(d, acc[s].delta);
         u += acc[s].updates;
     }
-    st->loss_delta = __dadd_rn(st->loss_delta, d);
-    st->updates += u;
-    if (rp.final_refit) return;
-    st->passes += 1;
-    double gain = __dsub_rn(st->prev_delta, st->loss_delta);
-    st->prev_delta = st->loss_delta;
-    if (u == 0ull || gain < rp.tol * __dadd_rn(st->loss_gptq, st->loss_delta)) st->done = 1;
+    if (rp.final_refit) {
+        st->loss_delta = __dadd_rn(st->loss_delta, d);
+        st->updates += u;
+        return;
+    }
+    apply_pass(st, d, u, rp.tol);
 }
 
 int launch_pass_end(const ChunkInfo* chunks_dev, int nchunks, const int* slice_begin_dev, const SliceAcc* acc_dev,

@@ -71,6 +71,10 @@ CASES = [
     ("large_sub_block", 64, 512, 2000, 35, Config(group=128, block=128, sub_block=128, row_chunk=64, passes=3)),
     ("block_256", 64, 512, 2000, 36, Config(group=128, block=256, row_chunk=64, passes=3)),
     ("group_512_refit", 32, 1024, 2500, 37, Config(group=512, block=128, sub_block=64, row_chunk=32, passes=2)),
+    # >= 2 x SM-count row chunks: the persistent repair kernel (all passes of a chunk in one CTA)
+    ("persistent_many_chunks", 2400, 96, 500, 38, Config(group=32, block=32, sub_block=16, row_chunk=8, passes=4)),
+    ("persistent_rc100_ragged", 30100, 64, 400, 39, Config(group=32, block=64, sub_block=32, row_chunk=100,
+                                                            passes=3)),
 ]
 
 
