@@ -451,6 +451,7 @@ def main():
         hb.run(0)
     torch.cuda.synchronize()
     e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+    e2e_prof = cdclq._lib.last_run_profile()
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -471,7 +472,9 @@ def main():
             "data": "synthetic (seeded bf16-valued weights and tokens; no checkpoints or datasets offline)",
             "config": workload_config(cfg),
             "e2e": {"value": total_weights / e2e_s, "unit": "weights/s", "seconds_per_model": e2e_s,
-                    "h2d_bytes_per_step": hb.h2d_bytes, "d2h_bytes_per_step": hb.d2h_bytes},
+                    "h2d_bytes_per_step": hb.h2d_bytes, "d2h_bytes_per_step": hb.d2h_bytes,
+                    "phases_ms": {k: e2e_prof[k] for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair",
+                                                           "ms_final")}},
             "gpu_launches": int(launches),
             "roofline": {
                 "kernel": "repair_pass_kernel (CDCL repair gradients on the FP32 SIMT GEMM core)",

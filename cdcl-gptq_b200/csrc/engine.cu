@@ -293,62 +293,125 @@ struct LayerPlan {
     size_t chunk0 = 0;
 };
 
-// Factorise a set of distinct inputs of one width (batched launches).  `entries` receive u/h32 pointers
-// that must already be allocated; `hdev` are the device Hessians (original order).
-static int factorize_batch(size_t n, const std::vector<const float*>& hdev, std::vector<PrepEntry*>& entries,
-                           const cdclq_config& cfg, cudaStream_t st) {
-    const size_t nitems = entries.size();
-    if (nitems == 0) return 0;
-    // Memory per item for the f64 work matrices; process in sub-batches bounded by free memory.
+// Factorisation of a set of distinct inputs of one width (one batch of launches on its own stream).
+struct FactorGroup {
+    size_t n = 0;
+    std::vector<const float*> hs;   // device Hessians (original order)
+    std::vector<PrepEntry*> es;     // receive damp_val; u/h32/perm_dev already allocated
+    size_t b0 = 0, nb = 0;          // current sub-batch
+    cudaStream_t st = nullptr;
+    std::unique_ptr<Arena> ar;
+    FactorStatus* status_dev = nullptr;
+    double* damp_dev = nullptr;
+    std::vector<FactorStatus> status;
+    std::vector<double> damp;
+};
+
+static size_t factor_item_bytes(size_t n) {
+    return 2 * n * n * sizeof(double) + 96 * n * sizeof(double) + n * sizeof(double) + 256;
+}
+
+static cudaStream_t pool_stream(size_t i) {
+    static thread_local std::vector<cudaStream_t> pool;
+    while (pool.size() <= i) {
+        cudaStream_t s = nullptr;
+        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        pool.push_back(s);
+    }
+    return pool[i];
+}
+
+// Enqueue items [g.b0, g.b0 + g.nb) of the group: prepare, Cholesky, triangular inverse, U scatter, and the
+// status / damping read-back (src/engine.rs:320-342, src/linalg.rs:362-375).
+static int factor_launch(FactorGroup& g, const cdclq_config& cfg) {
+    const size_t n = g.n, nb = g.nb;
+    g.ar.reset(new Arena(g.st));
+    Arena& ar = *g.ar;
+    std::vector<PrepItem> items(nb);
+    int rc = ar.alloc(&g.damp_dev, nb);
+    if (!rc) rc = ar.alloc(&g.status_dev, nb);
+    if (rc) return rc;
+    for (size_t i = 0; i < nb; i++) {
+        PrepEntry* pe = g.es[g.b0 + i];
+        PrepItem& it = items[i];
+        it.h = g.hs[g.b0 + i];
+        it.perm = pe->perm_dev;
+        if ((rc = ar.alloc(&it.hr, n * n))) return rc;
+        if ((rc = ar.alloc(&it.y, n * n))) return rc;
+        if ((rc = ar.alloc(&it.tbuf, 96 * n))) return rc;
+        if ((rc = ar.alloc(&it.dg, n))) return rc;
+        it.h32 = pe->h32;
+        it.u = pe->u;
+        it.damp_val = g.damp_dev + i;
+        it.status = g.status_dev + i;
+        CDCLQ_CUDA_TRY(cudaMemsetAsync(it.y, 0, n * n * sizeof(double), g.st));
+    }
+    PrepItem* items_dev = nullptr;
+    if ((rc = ar.alloc(&items_dev, nb))) return rc;
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(items_dev, items.data(), sizeof(PrepItem) * nb, cudaMemcpyHostToDevice, g.st));
+    if ((rc = launch_prepare(items_dev, (int)nb, (int)n, cfg.damp, g.st))) return rc;
+    if ((rc = launch_cholesky(items_dev, (int)nb, (int)n, g.st))) return rc;
+    if ((rc = launch_tri_inverse(items_dev, (int)nb, (int)n, g.st))) return rc;
+    if ((rc = launch_u_scatter(items_dev, (int)nb, (int)n, g.st))) return rc;
+    g.status.assign(nb, FactorStatus{0, -1, 0.0});
+    g.damp.assign(nb, 0.0);
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(g.status.data(), g.status_dev, sizeof(FactorStatus) * nb, cudaMemcpyDeviceToHost, g.st));
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(g.damp.data(), g.damp_dev, sizeof(double) * nb, cudaMemcpyDeviceToHost, g.st));
+    return 0;
+}
+
+static int factor_finish(FactorGroup& g) {
+    CDCLQ_CUDA_TRY(cudaStreamSynchronize(g.st));
+    g.ar.reset();
+    for (size_t i = 0; i < g.nb; i++) {
+        if (g.status[i].err) {
+            return set_error(CDCLQ_ERR_NOT_PD, "matrix is not positive definite (pivot " +
+                                                   std::to_string(g.status[i].pivot) + " = " +
+                                                   rust_exp(g.status[i].value) +
+                                                   "); increase --damp or check the Hessian");
+        }
+        g.es[g.b0 + i]->damp_val = g.damp[i];
+    }
+    return 0;
+}
+
+// Factorise every group.  Groups of different widths are independent: when their work matrices fit in
+// free memory together they run concurrently on separate streams (the latency-bound panel steps of one
+// width overlap the other's); otherwise each group runs alone in memory-bounded sub-batches.
+static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config& cfg, cudaStream_t st) {
+    if (groups.empty()) return 0;
     size_t freeb = 0, totalb = 0;
     cudaMemGetInfo(&freeb, &totalb);
-    const size_t per_item = 2 * n * n * sizeof(double) + 96 * n * sizeof(double) + n * sizeof(double) + 64;
     size_t budget = freeb > ((size_t)4 << 30) ? freeb - ((size_t)4 << 30) : freeb / 2;
-    size_t max_items = std::max<size_t>(1, budget / std::max<size_t>(per_item, 1));
-    for (size_t b0 = 0; b0 < nitems; b0 += max_items) {
-        size_t nb = std::min(max_items, nitems - b0);
-        Arena ar(st);
-        std::vector<PrepItem> items(nb);
-        double* damp_dev = nullptr;
-        FactorStatus* status_dev = nullptr;
-        int rc = ar.alloc(&damp_dev, nb);
-        if (!rc) rc = ar.alloc(&status_dev, nb);
-        if (rc) return rc;
-        for (size_t i = 0; i < nb; i++) {
-            PrepEntry* pe = entries[b0 + i];
-            PrepItem& it = items[i];
-            it.h = hdev[b0 + i];
-            it.perm = pe->perm_dev;
-            if ((rc = ar.alloc(&it.hr, n * n))) return rc;
-            if ((rc = ar.alloc(&it.y, n * n))) return rc;
-            if ((rc = ar.alloc(&it.tbuf, 96 * n))) return rc;
-            if ((rc = ar.alloc(&it.dg, n))) return rc;
-            it.h32 = pe->h32;
-            it.u = pe->u;
-            it.damp_val = damp_dev + i;
-            it.status = status_dev + i;
-            CDCLQ_CUDA_TRY(cudaMemsetAsync(it.y, 0, n * n * sizeof(double), st));
+    size_t need = 0;
+    for (auto& g : groups) need += factor_item_bytes(g.n) * g.hs.size();
+    cudaEvent_t ready = nullptr;
+    CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+    cudaEventRecord(ready, st);  // inputs uploaded / permutations copied on `st`
+    int rc = 0;
+    for (size_t k = 0; k < groups.size(); k++) {
+        groups[k].st = pool_stream(k);
+        cudaStreamWaitEvent(groups[k].st, ready, 0);
+    }
+    cudaEventDestroy(ready);
+    if (need <= budget) {
+        for (auto& g : groups) {
+            g.b0 = 0;
+            g.nb = g.hs.size();
+            if ((rc = factor_launch(g, cfg))) break;
         }
-        PrepItem* items_dev = nullptr;
-        if ((rc = ar.alloc(&items_dev, nb))) return rc;
-        CDCLQ_CUDA_TRY(cudaMemcpyAsync(items_dev, items.data(), sizeof(PrepItem) * nb, cudaMemcpyHostToDevice, st));
-        if ((rc = launch_prepare(items_dev, (int)nb, (int)n, cfg.damp, st))) return rc;
-        if ((rc = launch_cholesky(items_dev, (int)nb, (int)n, st))) return rc;
-        if ((rc = launch_tri_inverse(items_dev, (int)nb, (int)n, st))) return rc;
-        if ((rc = launch_u_scatter(items_dev, (int)nb, (int)n, st))) return rc;
-        std::vector<FactorStatus> status(nb);
-        std::vector<double> damp(nb);
-        CDCLQ_CUDA_TRY(cudaMemcpyAsync(status.data(), status_dev, sizeof(FactorStatus) * nb, cudaMemcpyDeviceToHost, st));
-        CDCLQ_CUDA_TRY(cudaMemcpyAsync(damp.data(), damp_dev, sizeof(double) * nb, cudaMemcpyDeviceToHost, st));
-        CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
-        for (size_t i = 0; i < nb; i++) {
-            if (status[i].err) {
-                return set_error(CDCLQ_ERR_NOT_PD, "matrix is not positive definite (pivot " +
-                                                       std::to_string(status[i].pivot) + " = " +
-                                                       rust_exp(status[i].value) +
-                                                       "); increase --damp or check the Hessian");
-            }
-            entries[b0 + i]->damp_val = damp[i];
+        for (auto& g : groups) {
+            int r2 = factor_finish(g);
+            if (!rc) rc = r2;
+        }
+        return rc;
+    }
+    for (auto& g : groups) {
+        size_t max_items = std::max<size_t>(1, budget / factor_item_bytes(g.n));
+        for (g.b0 = 0; g.b0 < g.hs.size(); g.b0 += max_items) {
+            g.nb = std::min(max_items, g.hs.size() - g.b0);
+            if ((rc = factor_launch(g, cfg))) return rc;
+            if ((rc = factor_finish(g))) return rc;
         }
     }
     return 0;
@@ -499,19 +562,21 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         }
         by_n[n].push_back(k);
     }
+    std::vector<FactorGroup> groups;
     for (auto& kv : by_n) {
-        std::vector<const float*> hs;
-        std::vector<PrepEntry*> es;
+        FactorGroup g;
+        g.n = kv.first;
         for (size_t k : kv.second) {
-            hs.push_back(h_dev[prep_input[k]]);
-            es.push_back(&preps[k]);
+            g.hs.push_back(h_dev[prep_input[k]]);
+            g.es.push_back(&preps[k]);
         }
-        if ((rc = factorize_batch(kv.first, hs, es, cfg, st))) {
-            if (cache) {
-                for (auto& pe : preps) pe.release();
-            }
-            return rc;
+        groups.push_back(std::move(g));
+    }
+    if ((rc = factorize_groups(groups, cfg, st))) {
+        if (cache) {
+            for (auto& pe : preps) pe.release();
         }
+        return rc;
     }
     if (cache && !preps.empty()) {
         cache->e = preps[0];

@@ -84,102 +84,96 @@ struct CholArgs {
     FactorStatus* status;
 };
 
-__global__ void __launch_bounds__(256) chol_diag_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
-    extern __shared__ double sblk[];  // [kb][kb+1]
+// One thread per row of the 96-row block (rows past kb are identity padding and never stored); the row lives
+// in registers.  Per column j: the owner of row j takes the square root of its diagonal (after every earlier
+// term was subtracted) and checks the pivot; rows below divide their column-j entry and publish it; then each
+// row subtracts its a[i][j] * a[c][j] terms for j < c <= i.  Two barriers per column.
+__global__ void __launch_bounds__(128) chol_diag_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    __shared__ double colj[2][NB];
+    __shared__ double dsh;
+    __shared__ int bad;
     const CholArgs ar = args[blockIdx.x];
     if (ar.status->err) return;
-    const int ld = kb + 1, tid = threadIdx.x, nt = blockDim.x;
     double* A = ar.a;
-    for (int idx = tid; idx < kb * kb; idx += nt) {
-        int i = idx / kb, c = idx - i * kb;
-        if (c <= i) sblk[i * ld + c] = A[(int64_t)(k + i) * n + (k + c)];
-    }
-    __shared__ int bad;
-    __shared__ double dj;
-    if (tid == 0) bad = 0;
+    const int i = threadIdx.x;  // block row (threads >= NB idle through the loop)
+    double x[NB];
+#pragma unroll
+    for (int c = 0; c < NB; c++)
+        x[c] = (i < kb && c <= i) ? A[(int64_t)(k + i) * n + (k + c)] : ((c == i) ? 1.0 : 0.0);
+    if (i == 0) bad = 0;
     __syncthreads();
-    for (int j = 0; j < kb; j++) {
-        if (tid == 0) {
-            double d = sblk[j * ld + j];
-            if (!(d > 0.0) || !isfinite(d)) {
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+        if (i == j) {
+            double d = x[j];
+            if (j < kb && (!(d > 0.0) || !isfinite(d))) {
                 bad = 1;
                 ar.status->err = 1;
                 ar.status->pivot = k + j;
                 ar.status->value = d;
             } else {
                 d = __dsqrt_rn(d);
-                sblk[j * ld + j] = d;
-                dj = d;
+                x[j] = d;
+                dsh = d;
             }
         }
         __syncthreads();
         if (bad) return;
-        const double d = dj;
-        for (int i = j + 1 + tid; i < kb; i += nt) sblk[i * ld + j] = __ddiv_rn(sblk[i * ld + j], d);
-        __syncthreads();
-        // pairs (i, c) with j < c <= i < kb, enumerated as i = j+1+pi, c = j+1+pc, pc <= pi
-        const int m = kb - j - 1;
-        const int npairs = m * (m + 1) / 2;
-        for (int p = tid; p < npairs; p += nt) {
-            int pi = (int)((sqrt(8.0 * p + 1.0) - 1.0) * 0.5);
-            while ((pi + 1) * (pi + 2) / 2 <= p) pi++;
-            while (pi * (pi + 1) / 2 > p) pi--;
-            int pc = p - pi * (pi + 1) / 2;
-            int i = j + 1 + pi, c = j + 1 + pc;
-            sblk[i * ld + c] = __dsub_rn(sblk[i * ld + c], __dmul_rn(sblk[i * ld + j], sblk[c * ld + j]));
+        if (i > j && i < NB) {
+            x[j] = __ddiv_rn(x[j], dsh);
+            colj[j & 1][i] = x[j];
         }
         __syncthreads();
+        if (i > j && i < NB) {
+#pragma unroll
+            for (int c = 0; c < NB; c++)  // constant trip count: unrolls into registers once j is known
+                if (c > j && c <= i) x[c] = __dsub_rn(x[c], __dmul_rn(x[j], colj[j & 1][c]));
+        }
     }
-    for (int idx = tid; idx < kb * kb; idx += nt) {
-        int i = idx / kb, c = idx - i * kb;
-        if (c <= i) A[(int64_t)(k + i) * n + (k + c)] = sblk[i * ld + c];
+    if (i < kb) {
+#pragma unroll
+        for (int c = 0; c < NB; c++)
+            if (c <= i) A[(int64_t)(k + i) * n + (k + c)] = x[c];
     }
 }
 
-// Cholesky step 2 (src/linalg.rs:232-241): panel rows i >= kend solve X L_kk^T = A_panel.  One warp per row,
-// lane l owns columns l, l+32, l+64; the reference's per-row loop `s -= row[t]*top[j][t]; row[j] = s/top[j][j]`
-// becomes: row[j] final -> broadcast -> row[c] -= row[j] * L[c][j] for c > j (same per-element order).
-__global__ void __launch_bounds__(256) chol_panel_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
-    extern __shared__ double lt[];  // [kb][kb]: lt[j][c] = L[k+c][k+j] (c >= j), the transposed block
+// Cholesky step 2 (src/linalg.rs:232-241): panel rows i >= kend solve X L_kk^T = A_panel, one thread per row
+// with the row in registers: row[j] = (row[j] - sum_t row[t] L[j][t]) / L[j][j], the terms subtracted in
+// increasing t as soon as row[t] is final (the reference's per-element order).  The diagonal block is read
+// transposed from shared memory (every thread reads the same element: broadcasts); columns past kb are
+// identity padding.
+__global__ void __launch_bounds__(128) chol_panel_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    extern __shared__ double lt[];  // [NB][NB]: lt[j][c] = L[k+c][k+j] for j <= c < kb
     const CholArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
     double* A = ar.a;
     const int kend = k + kb;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int idx = tid; idx < kb * kb; idx += blockDim.x) {
-        int c = idx / kb, j = idx - c * kb;
-        lt[j * kb + c] = (j <= c) ? A[(int64_t)(k + c) * n + (k + j)] : 0.0;
+    for (int idx = threadIdx.x; idx < NB * NB; idx += blockDim.x) {
+        int j = idx / NB, c = idx - j * NB;
+        double v;
+        if (c < kb && j < kb)
+            v = (j <= c) ? A[(int64_t)(k + c) * n + (k + j)] : 0.0;
+        else
+            v = (c == j) ? 1.0 : 0.0;
+        lt[idx] = v;
     }
     __syncthreads();
-    const int rows_per_cta = 64;
-    const int rbeg = kend + blockIdx.x * rows_per_cta;
-    for (int rr = warp; rr < rows_per_cta; rr += 8) {
-        const int i = rbeg + rr;
-        if (i >= n) break;
-        double* row = A + (int64_t)i * n + k;
-        double x0 = (lane < kb) ? row[lane] : 0.0;
-        double x1 = (lane + 32 < kb) ? row[lane + 32] : 0.0;
-        double x2 = (lane + 64 < kb) ? row[lane + 64] : 0.0;
-        for (int j = 0; j < kb; j++) {
-            const int owner = j & 31, slot = j >> 5;
-            double xj;
-            if (lane == owner) {
-                double v = slot == 0 ? x0 : (slot == 1 ? x1 : x2);
-                v = __ddiv_rn(v, lt[j * kb + j]);
-                if (slot == 0) x0 = v; else if (slot == 1) x1 = v; else x2 = v;
-                xj = v;
-            }
-            xj = __shfl_sync(0xffffffffu, xj, owner);
-            const double* lrow = lt + j * kb;
-            int c0 = lane, c1 = lane + 32, c2 = lane + 64;
-            if (c0 > j && c0 < kb) x0 = __dsub_rn(x0, __dmul_rn(xj, lrow[c0]));
-            if (c1 > j && c1 < kb) x1 = __dsub_rn(x1, __dmul_rn(xj, lrow[c1]));
-            if (c2 > j && c2 < kb) x2 = __dsub_rn(x2, __dmul_rn(xj, lrow[c2]));
-        }
-        if (lane < kb) row[lane] = x0;
-        if (lane + 32 < kb) row[lane + 32] = x1;
-        if (lane + 64 < kb) row[lane + 64] = x2;
+    const int i = kend + blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    double* row = A + (int64_t)i * n + k;
+    double x[NB];
+#pragma unroll
+    for (int c = 0; c < NB; c++) x[c] = (c < kb) ? row[c] : 0.0;
+#pragma unroll
+    for (int j = 0; j < NB; j++) {
+        x[j] = __ddiv_rn(x[j], lt[j * NB + j]);
+#pragma unroll
+        for (int c = 0; c < NB; c++)  // constant trip count: unrolls into registers once j is known
+            if (c > j) x[c] = __dsub_rn(x[c], __dmul_rn(x[j], lt[j * NB + c]));
     }
+#pragma unroll
+    for (int c = 0; c < NB; c++)
+        if (c < kb) row[c] = x[c];
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -324,15 +318,13 @@ static int run_cholesky(const CholArgs* args_dev, int nitems, int n, cudaStream_
     for (int k = 0; k < n; k += NB) {
         int kb = min(NB, n - k);
         int kend = k + kb;
-        size_t smem1 = (size_t)kb * (kb + 1) * sizeof(double);
-        cudaFuncSetAttribute(chol_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
-        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 256, smem1, st, args_dev, n, k, kb);
+        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 128, 0, st, args_dev, n, k, kb);
         if (kend < n) {
             int rows_below = n - kend;
-            size_t smem2 = (size_t)kb * kb * sizeof(double);
+            size_t smem2 = (size_t)NB * NB * sizeof(double);
             cudaFuncSetAttribute(chol_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
-            dim3 gp((rows_below + 63) / 64, nitems);
-            CDCLQ_LAUNCH(chol_panel_kernel, gp, 256, smem2, st, args_dev, n, k, kb);
+            dim3 gp((rows_below + 127) / 128, nitems);
+            CDCLQ_LAUNCH(chol_panel_kernel, gp, 128, smem2, st, args_dev, n, k, kb);
             long long T = (rows_below + 63) / 64;
             dim3 gt((unsigned)(T * (T + 1) / 2), nitems);
             CDCLQ_LAUNCH(chol_trail_kernel, gt, 256, 0, st, args_dev, n, k, kb);
@@ -354,31 +346,33 @@ struct TriArgs {
 };
 
 __global__ void __launch_bounds__(128) tri_diag_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
-    extern __shared__ double tsm[];
+    extern __shared__ double Ls[];  // [NB][NB] lower block, identity past w
     const TriArgs ar = args[blockIdx.x];
     if (ar.status->err) return;
-    double* Ls = tsm;                 // [w][w] lower block
-    double* Acc = tsm + (size_t)w * w;  // [w][w+1]: Acc[i][c]
-    const int ldc = w + 1, tid = threadIdx.x;
-    for (int idx = tid; idx < w * w; idx += blockDim.x) {
-        int i = idx / w, c = idx - i * w;
-        Ls[idx] = (c <= i) ? ar.l[(int64_t)(s + i) * n + (s + c)] : 0.0;
-        Acc[i * ldc + c] = 0.0;
+    for (int idx = threadIdx.x; idx < NB * NB; idx += blockDim.x) {
+        int i = idx / NB, c = idx - i * NB;
+        double v;
+        if (i < w && c < w)
+            v = (c <= i) ? ar.l[(int64_t)(s + i) * n + (s + c)] : 0.0;
+        else
+            v = (i == c) ? 1.0 : 0.0;
+        Ls[idx] = v;
     }
     __syncthreads();
-    const int c = tid;
-    if (c < w) {
-        for (int t = c; t < w; t++) {
-            double yt = (t == c) ? __ddiv_rn(1.0, Ls[t * w + t]) : __ddiv_rn(-Acc[t * ldc + c], Ls[t * w + t]);
-            Acc[t * ldc + c] = yt;  // column c, row t is now final
-            for (int i = t + 1; i < w; i++)
-                Acc[i * ldc + c] = __dadd_rn(Acc[i * ldc + c], __dmul_rn(Ls[i * w + t], yt));
+    const int c = threadIdx.x;  // column of the block inverse owned by this thread
+    if (c >= w) return;
+    double acc[NB];
+#pragma unroll
+    for (int i = 0; i < NB; i++) acc[i] = 0.0;
+#pragma unroll
+    for (int t = 0; t < NB; t++) {
+        if (t >= c) {
+            const double yt = (t == c) ? __ddiv_rn(1.0, Ls[t * NB + t]) : __ddiv_rn(-acc[t], Ls[t * NB + t]);
+            if (t < w) ar.y[(int64_t)(s + t) * n + (s + c)] = yt;
+#pragma unroll
+            for (int i = 0; i < NB; i++)  // constant trip count: unrolls into registers once t is known
+                if (i > t) acc[i] = __dadd_rn(acc[i], __dmul_rn(Ls[i * NB + t], yt));
         }
-    }
-    __syncthreads();
-    for (int idx = tid; idx < w * w; idx += blockDim.x) {
-        int i = idx / w, cc = idx - i * w;
-        if (cc <= i) ar.y[(int64_t)(s + i) * n + (s + cc)] = Acc[i * ldc + cc];
     }
 }
 
@@ -454,7 +448,7 @@ __global__ void __launch_bounds__(256) tri_gemm2_kernel(const TriArgs* __restric
 static int run_tri_inverse(const TriArgs* args_dev, int nitems, int n, cudaStream_t st) {
     for (int s = 0; s < n; s += NB) {
         int w = min(NB, n - s);
-        size_t smem = (size_t)w * w * sizeof(double) + (size_t)w * (w + 1) * sizeof(double);
+        size_t smem = (size_t)NB * NB * sizeof(double);
         cudaFuncSetAttribute(tri_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         CDCLQ_LAUNCH(tri_diag_kernel, nitems, 128, smem, st, args_dev, n, s, w);
         if (s > 0) {
