@@ -903,6 +903,21 @@ static int ensure_device() {
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count == 0)
         return set_error(CDCLQ_ERR_CUDA, std::string("no CUDA device available: ") + cudaGetErrorString(e));
+    // The per-call buffers come from the device's default stream-ordered pool.  Keep freed pool memory cached
+    // instead of returning it to the driver at every synchronisation (release threshold 0 by default), so a
+    // repeated call does not pay for re-mapping tens of GB.
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+        static bool configured[64] = {false};
+        if (!configured[dev]) {
+            cudaMemPool_t pool;
+            if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+                uint64_t threshold = UINT64_MAX;
+                cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+            }
+            configured[dev] = true;
+        }
+    }
     return 0;
 }
 
