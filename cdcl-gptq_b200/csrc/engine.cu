@@ -777,13 +777,20 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     }
     // Many row chunks: one persistent launch, chunks scheduled heaviest first.  Few row chunks: one launch per
     // pass over 64-row slices, so a chunk's rows spread over several SMs.  Both give identical results.
-    const bool persistent = total_chunks >= (size_t)(2 * sms);
+    size_t max_rows = 0;
+    for (auto& P : plans) max_rows = std::max(max_rows, std::min(P.rc, P.d_out));
+    const bool persistent = total_chunks >= (size_t)sms;
     if (cdcl && (rp.do_cd || rp.do_refit) && persistent) {
         int* counter = nullptr;
         if ((rc = ar.alloc(&counter, 1))) return rc;
-        if ((rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
-                                           (int)std::min<size_t>(cfg.sub_block, maxn), counter, st)))
-            return rc;
+        // chunks of more than one 64-row tile: a 2-CTA cluster per chunk
+        if (max_rows > 64 && max_rows <= 2048)
+            rc = launch_repair_cluster(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
+                                       (int)std::min<size_t>(cfg.sub_block, maxn), counter, st);
+        else
+            rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
+                                          (int)std::min<size_t>(cfg.sub_block, maxn), counter, st);
+        if (rc) return rc;
         repair_launches = 1;
         pev.record(4, st);
     } else if (cdcl && (rp.do_cd || rp.do_refit)) {

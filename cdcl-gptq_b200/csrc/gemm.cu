@@ -34,7 +34,9 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int m, int n, int k, float a
         AGlobal A{a + (int64_t)r0 * lda, lda, min(GEMM_RT, m - r0), k, (lda % 4 == 0) && (((uintptr_t)a & 15) == 0)};
         gemm_loader_a<8>(acc, A, B, k, stage);
     }
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int tid = threadIdx.x;
+    int ty, tx;
+    gemm_coords(tid, ty, tx);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         int r = r0 + ty * 4 + i;

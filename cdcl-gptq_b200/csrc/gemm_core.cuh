@@ -26,6 +26,16 @@ constexpr int GEMM_RT = 64;      // rows per CTA tile
 constexpr int GEMM_ALD = 68;     // k-major A row stride (64 rows + 4 pad, keeps 16-byte alignment)
 constexpr int GEMM_THREADS = 256;
 
+// Thread coordinates inside the 16 x 16 thread grid of a CTA tile.  Each warp covers 8 (ty) x 4 (tx)
+// threads, so per k-step its A fragments are 32 consecutive rows (one 128-byte shared-memory wavefront) and its
+// B fragments 4 x 4 consecutive columns (one 64-byte broadcast wavefront per 16-byte load): 3 wavefronts per
+// warp and k at TN = 8 instead of 5 with a 2 x 16 warp shape.
+__device__ __forceinline__ void gemm_coords(int tid, int& ty, int& tx) {
+    const int lane = tid & 31, warp = tid >> 5;
+    ty = ((warp >> 2) << 3) | (lane >> 2);
+    tx = ((warp & 3) << 2) | (lane & 3);
+}
+
 template <int TN>
 struct ColMap {
     // column (within the CTA tile) of the thread's j-th accumulator
@@ -162,7 +172,9 @@ struct BGlobal {
 // `stage` points at gemm_stage_floats<TN>() floats of shared memory.  Ends with a __syncthreads().
 template <int TN>
 __device__ void gemm_global_a(float (&acc)[4][TN], const AGlobal& A, const BGlobal<TN>& B, int K, float* stage) {
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int tid = threadIdx.x;
+    int ty, tx;
+    gemm_coords(tid, ty, tx);
     float* const As0 = stage;                            // As[buf] = As0 + buf * KT*ALD
     float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;
@@ -194,7 +206,9 @@ __device__ void gemm_global_a(float (&acc)[4][TN], const AGlobal& A, const BGlob
 // by the caller.  Ends with a __syncthreads().
 template <int TN>
 __device__ void gemm_smem_a(float (&acc)[4][TN], const float* As_full, const BGlobal<TN>& B, int K, float* stage) {
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int tid = threadIdx.x;
+    int ty, tx;
+    gemm_coords(tid, ty, tx);
     float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;
     float rb[PER];
@@ -263,7 +277,9 @@ struct AGlobalT {
 // __syncthreads().
 template <int TN, class AL>
 __device__ void gemm_loader_a(float (&acc)[4][TN], const AL& A, const BGlobal<TN>& B, int K, float* stage) {
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int tid = threadIdx.x;
+    int ty, tx;
+    gemm_coords(tid, ty, tx);
     float* const As0 = stage;                            // As[buf] = As0 + buf * KT*ALD
     float* const Bs0 = stage + 2 * GEMM_KT * GEMM_ALD;   // Bs[buf] = Bs0 + buf * KT*16*TN
     constexpr int PER = BGlobal<TN>::PER;

@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
 
         // ---- lazy update of the columns past the block (src/engine.rs:452-471): w -= err1 * U[i1:i2, i2:]
         if (i2 < n) {
-            const int ty = tid >> 4, tx = tid & 15;
+            int ty, tx;
+            gemm_coords(tid, ty, tx);
             for (int c0 = i2; c0 < n; c0 += 128) {
                 float acc[4][8];
 #pragma unroll

@@ -123,6 +123,9 @@ size_t repair_smem_bytes(int g, int sbw);
 // All passes + final refit of every chunk in one launch (chunks taken from *counter_dev, in array order).
 int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
                              int* counter_dev, cudaStream_t st);
+// Same with a 2-CTA cluster per chunk (chunks of more than 64 rows, at most 2048 rows).
+int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                          int* counter_dev, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------------------
 // Generic f32 GEMM with the fixed order: C = alpha*A*B (+ beta*C), A row-major or transposed (gemm.cu)

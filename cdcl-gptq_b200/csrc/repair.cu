@@ -11,6 +11,8 @@
 //   * the block gradients G = E H[:, c0:c1] run on the FP32 GEMM core (fixed k order, bit-exact);
 //   * the sequential per-row work (refit numerators/denominators, the coordinate sweep with its rank-1
 //     gradient updates) runs one thread per row, in the reference's order, on shared-memory tiles.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "gemm_core.cuh"
 #include "kernels.h"
@@ -115,7 +117,9 @@ struct ACodes {
 template <class AL>
 __device__ void gemm_to_tile(const AL& A, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
                              float* stage) {
-    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int tid = threadIdx.x;
+    int ty, tx;
+    gemm_coords(tid, ty, tx);
     const bool vec = (ldb % 4 == 0) && (col0 % 4 == 0);
     if (wd > 64) {
         float acc[4][8];
@@ -533,6 +537,100 @@ __global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkIn
     }
 }
 
+// Mode C - persistent clusters: a cluster of 2 CTAs takes a whole row chunk (heaviest first); CTA rank r
+// handles the chunk's 64-row tiles r, r+2, ...  A row chunk's passes are the latency-critical unit (a
+// 128-row down_proj chunk does 7.5x the work of a 2048-wide one), and splitting its rows over two SMs halves
+// that critical path.  At the end of each pass the tiles' partial sums are written into rank 0's shared
+// memory (distributed shared memory), rank 0 adds them in tile order - the order of modes A and B - applies
+// the stop rule and writes the decision back into rank 1; hardware cluster barriers order these steps.
+constexpr int RP_MAX_TILES = 32;  // chunks up to 2048 rows
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
+    repair_cluster_kernel(const ChunkInfo* __restrict__ chunks, int nchunks, RepairParams rp, int* __restrict__ counter) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int s_chunk, s_done;
+    __shared__ ChunkInfo ci;
+    __shared__ double s_tile_delta[RP_MAX_TILES];
+    __shared__ unsigned long long s_tile_upd[RP_MAX_TILES];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int tid = threadIdx.x;
+    int* chunk0 = cluster.map_shared_rank(&s_chunk, 0);
+    int* done1 = cluster.map_shared_rank(&s_done, 1);
+    double* tdelta0 = cluster.map_shared_rank(&s_tile_delta[0], 0);
+    unsigned long long* tupd0 = cluster.map_shared_rank(&s_tile_upd[0], 0);
+    for (;;) {
+        if (rank == 0 && tid == 0) s_chunk = atomicAdd(counter, 1);
+        cluster.sync();
+        const int c = *chunk0;
+        if (tid == 0 && c < nchunks) ci = chunks[c];
+        cluster.sync();  // every rank has read rank 0's s_chunk before anyone may leave or overwrite it
+        if (c >= nchunks) return;
+        ChunkState* st = ci.st;
+        const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
+        const int ntiles = (ci.rows + RP_ROWS - 1) / RP_ROWS;
+        if (tid == 0) s_done = st->done;
+        __syncthreads();
+        for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
+            for (int t = rank; t < ntiles; t += 2) {
+                const int r0 = t * RP_ROWS, rs = min(RP_ROWS, ci.rows - r0);
+                double my_delta = 0.0;
+                unsigned long long my_upd = 0ull;
+                if (rp.do_refit) refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+                if (rp.do_cd) cd_tile(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+                double d;
+                unsigned long long u;
+                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                if (tid == 0) {
+                    tdelta0[t] = d;
+                    tupd0[t] = u;
+                }
+            }
+            cluster.sync();  // all tile partials are in rank 0
+            if (rank == 0 && tid == 0) {
+                double pd = 0.0;
+                unsigned long long pu = 0ull;
+                for (int t = 0; t < ntiles; t++) {
+                    pd = __dadd_rn(pd, s_tile_delta[t]);
+                    pu += s_tile_upd[t];
+                }
+                apply_pass(st, pd, pu, rp.tol);
+                s_done = st->done;
+                *done1 = st->done;
+            }
+            cluster.sync();  // the decision is visible in both ranks
+        }
+        if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
+            for (int t = rank; t < ntiles; t += 2) {
+                const int r0 = t * RP_ROWS, rs = min(RP_ROWS, ci.rows - r0);
+                double my_delta = 0.0;
+                unsigned long long my_upd = 0ull;
+                refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+                double d;
+                unsigned long long u;
+                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                if (tid == 0) {
+                    tdelta0[t] = d;
+                    tupd0[t] = u;
+                }
+            }
+            cluster.sync();
+            if (rank == 0 && tid == 0) {
+                double fd = 0.0;
+                unsigned long long fu = 0ull;
+                for (int t = 0; t < ntiles; t++) {
+                    fd = __dadd_rn(fd, s_tile_delta[t]);
+                    fu += s_tile_upd[t];
+                }
+                st->loss_delta = __dadd_rn(st->loss_delta, fd);
+                st->updates += fu;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 static int set_repair_smem(const void* fn, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     return e == cudaSuccess ? 0 : cuda_error(e, "repair smem attribute");
@@ -547,6 +645,26 @@ int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev,
     CDCLQ_LAUNCH(repair_pass_kernel, nslices, 256, smem, st, chunks_dev, slices_dev, acc_dev, rp);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_pass_kernel launch");
+}
+
+int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                          int* counter_dev, cudaStream_t st) {
+    if (nchunks == 0) return 0;
+    size_t smem = repair_smem_bytes(g, sbw);
+    int rc = set_repair_smem((const void*)repair_cluster_kernel, smem);
+    if (rc) return rc;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_cluster_kernel, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    int clusters = sms * per_sm / 2;
+    if (clusters > nchunks) clusters = nchunks;
+    if (clusters < 1) clusters = 1;
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
+    CDCLQ_LAUNCH(repair_cluster_kernel, 2 * clusters, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_cluster_kernel launch");
 }
 
 int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
