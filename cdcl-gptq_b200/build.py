@@ -3,7 +3,7 @@
     python cdcl-gptq_b200/build.py [--verbose] [--force]
 
 nvcc cross-compiles for sm_100a without a GPU.  Each .cu file is compiled to an object in parallel (objects
-are reused while neither the source nor a shared header changed), then linked into the shared library.
+are reused while neither the source nor a header it includes changed), then linked into the shared library.
 Flags that matter for the numerics:
   -fmad=false   no implicit a*b+c contraction: the reference (Rust) never contracts, so every rounding outside
                 the explicit __fmaf_rn / __fma_rn of the fixed GEMM order must stay a separate multiply and add;
@@ -32,9 +32,32 @@ def nvcc_path():
     return "nvcc"
 
 
-def _deps_mtime():
-    deps = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "cdclq.h"),
-                                                        os.path.abspath(__file__)]
+def _includes(path, seen):
+    """Local headers a file includes, transitively (quoted includes found in csrc/ or include/)."""
+    try:
+        text = open(path).read()
+    except OSError:
+        return seen
+    for line in text.splitlines():
+        line = line.strip()
+        if line.startswith("#include \""):
+            name = line.split('"')[1]
+            for d in (CSRC, os.path.join(ROOT, "include")):
+                h = os.path.join(d, name)
+                if os.path.exists(h) and h not in seen:
+                    seen.add(h)
+                    _includes(h, seen)
+                    break
+    return seen
+
+
+def _deps_mtime(src=None):
+    """Newest modification time among the headers `src` includes (all shared headers when src is None)."""
+    if src is None:
+        deps = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "cdclq.h")]
+    else:
+        deps = sorted(_includes(os.path.join(CSRC, src), set()))
+    deps.append(os.path.abspath(__file__))
     return max(os.path.getmtime(d) for d in deps if os.path.exists(d))
 
 
@@ -42,20 +65,19 @@ def _obj(src):
     return os.path.join(OBJ, src.replace(".cu", ".o"))
 
 
-def _stale(src, dep_t):
+def _stale(src):
     o = _obj(src)
     if not os.path.exists(o):
         return True
     t = os.path.getmtime(o)
-    return os.path.getmtime(os.path.join(CSRC, src)) > t or dep_t > t
+    return os.path.getmtime(os.path.join(CSRC, src)) > t or _deps_mtime(src) > t
 
 
 def needs_rebuild():
     if not os.path.exists(OUT):
         return True
-    dep_t = _deps_mtime()
     t = os.path.getmtime(OUT)
-    return any(_stale(s, dep_t) for s in SOURCES) or any(os.path.getmtime(_obj(s)) > t for s in SOURCES)
+    return any(_stale(s) for s in SOURCES) or any(os.path.getmtime(_obj(s)) > t for s in SOURCES)
 
 
 def _compile(src, verbose):
@@ -71,8 +93,7 @@ def build(verbose=False, force=False):
     if not force and not needs_rebuild():
         return OUT
     os.makedirs(OBJ, exist_ok=True)
-    dep_t = _deps_mtime()
-    todo = [s for s in SOURCES if force or _stale(s, dep_t)]
+    todo = [s for s in SOURCES if force or _stale(s)]
     failed = []
     with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(todo), os.cpu_count() or 4))) as ex:
         for src, r in ex.map(lambda s: _compile(s, verbose), todo):

@@ -97,7 +97,7 @@ static int check_tiling(const cdclq_config& c, size_t n) {
     if (phase1_smem_bytes((int)std::min<size_t>(c.block, n)) > (size_t)maxsm)
         return set_error(CDCLQ_ERR_CONFIG, "block " + std::to_string(c.block) +
                                                " exceeds the GPTQ kernel's shared-memory tile (max 320 columns)");
-    if (repair_smem_bytes((int)g, (int)std::min<size_t>(c.sub_block, n)) > (size_t)maxsm)
+    if (repair_smem_bytes((int)g, (int)std::min<size_t>(c.sub_block, n), 64) > (size_t)maxsm)
         return set_error(CDCLQ_ERR_CONFIG, "sub_block " + std::to_string(c.sub_block) +
                                                " exceeds the repair kernel's shared-memory tile (max 256 columns)");
     if (n > 65535) return set_error(CDCLQ_ERR_CONFIG, "d_in above 65535 is not supported");
@@ -776,20 +776,22 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     }
     // Many row chunks: one persistent launch, chunks scheduled heaviest first.  Few row chunks: one launch per
-    // pass over 64-row slices, so a chunk's rows spread over several SMs.  Both give identical results.
+    // pass over 64-row slices, so a chunk's rows spread over several SMs.  All modes give identical codes,
+    // scales and pass counts; the f64 loss bookkeeping adds per-tile sums, so its last bits depend on the tile
+    // height.
     size_t max_rows = 0;
     for (auto& P : plans) max_rows = std::max(max_rows, std::min(P.rc, P.d_out));
     const bool persistent = total_chunks >= (size_t)sms;
     if (cdcl && (rp.do_cd || rp.do_refit) && persistent) {
         int* counter = nullptr;
         if ((rc = ar.alloc(&counter, 1))) return rc;
-        // chunks of more than one 64-row tile: a 2-CTA cluster per chunk
-        if (max_rows > 64 && max_rows <= 2048)
-            rc = launch_repair_cluster(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
-                                       (int)std::min<size_t>(cfg.sub_block, maxn), counter, st);
+        const int g0 = (int)plans[0].g, sbw0 = (int)std::min<size_t>(cfg.sub_block, maxn);
+        const int bm = repair_tile_rows(g0, sbw0, (int)max_rows);
+        // chunks of more than one row tile: a 2-CTA cluster per chunk
+        if (max_rows > (size_t)bm && max_rows <= (size_t)bm * RP_MAX_TILES_PER_CHUNK)
+            rc = launch_repair_cluster(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);
         else
-            rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, (int)plans[0].g,
-                                          (int)std::min<size_t>(cfg.sub_block, maxn), counter, st);
+            rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);
         if (rc) return rc;
         repair_launches = 1;
         pev.record(4, st);

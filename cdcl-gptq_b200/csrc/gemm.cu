@@ -11,43 +11,62 @@
 
 namespace cdclq {
 
-// C[i][j] = alpha * acc (beta == 0) or alpha * acc + beta * C[i][j]; tile 64 x 128.
+// C[i][j] = alpha * acc (beta == 0) or alpha * acc + beta * C[i][j]; CTA tile 128 x 128.
+using SgemmTile = Tile<128, 128, 8>;
+
+__device__ __forceinline__ float sgemm_out(float alpha, float beta, float acc, float old) {
+    const float v = __fmul_rn(alpha, acc);
+    return (beta == 0.0f) ? v : __fadd_rn(v, __fmul_rn(beta, old));
+}
+
 template <bool AT>
 __global__ void __launch_bounds__(256) sgemm_kernel(int m, int n, int k, float alpha, const float* a, int64_t lda,
                                                     const float* b, int64_t ldb, float beta, float* c, int64_t ldc,
                                                     int lower_only) {
-    __shared__ __align__(16) float stage[gemm_stage_floats<8>()];
-    const int r0 = blockIdx.y * GEMM_RT, c0 = blockIdx.x * 128;
-    if (lower_only && c0 > r0 + GEMM_RT - 1) return;  // tile entirely above the diagonal
-    float acc[4][8];
+    using S = SgemmTile;
+    __shared__ __align__(16) float stage[S::STAGE_FLOATS];
+    const int r0 = blockIdx.y * S::BM, c0 = blockIdx.x * S::BN;
+    if (lower_only && c0 > r0 + S::BM - 1) return;  // tile entirely above the diagonal
+    float acc[S::TM][S::TN];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < S::TM; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-    BGlobal<8> B{b, ldb, (int64_t)c0, min(128, n - c0), k, (ldb % 4 == 0) && (c0 % 4 == 0) &&
-                                                           (((uintptr_t)b & 15) == 0)};
+        for (int j = 0; j < S::TN; j++) acc[i][j] = 0.0f;
+    BGlobal<S> B{b, ldb, (int64_t)c0, min(S::BN, n - c0), k,
+                 (ldb % 4 == 0) && (c0 % 4 == 0) && (((uintptr_t)b & 15) == 0)};
     if (AT) {
-        AGlobalT A{a, lda, (int64_t)r0, min(GEMM_RT, m - r0), k, (lda % 4 == 0) && (r0 % 4 == 0) &&
-                                                                  (((uintptr_t)a & 15) == 0)};
-        gemm_loader_a<8>(acc, A, B, k, stage);
+        AGlobalT<S> A{a, lda, (int64_t)r0, min(S::BM, m - r0), k,
+                      (lda % 4 == 0) && (r0 % 4 == 0) && (((uintptr_t)a & 15) == 0)};
+        gemm_loader_a<S>(acc, A, B, k, stage);
     } else {
-        AGlobal A{a + (int64_t)r0 * lda, lda, min(GEMM_RT, m - r0), k, (lda % 4 == 0) && (((uintptr_t)a & 15) == 0)};
-        gemm_loader_a<8>(acc, A, B, k, stage);
+        AGlobal<S> A{a + (int64_t)r0 * lda, lda, min(S::BM, m - r0), k, (lda % 4 == 0) && (((uintptr_t)a & 15) == 0)};
+        gemm_loader_a<S>(acc, A, B, k, stage);
     }
-    const int tid = threadIdx.x;
     int ty, tx;
-    gemm_coords(tid, ty, tx);
+    gemm_coords(threadIdx.x, ty, tx);
+    const bool vec = (ldc % 4 == 0) && (((uintptr_t)c & 15) == 0);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int r = r0 + ty * 4 + i;
+    for (int i = 0; i < S::TM; i++) {
+        const int r = r0 + TileMap<S>::row(ty, i);
         if (r >= m) continue;
+        float* crow = c + (int64_t)r * ldc;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            int cc = c0 + ColMap<8>::col(tx, j);
-            if (cc >= n) continue;
-            float* p = c + (int64_t)r * ldc + cc;
-            float v = __fmul_rn(alpha, acc[i][j]);
-            *p = (beta == 0.0f) ? v : __fadd_rn(v, __fmul_rn(beta, *p));
+        for (int v = 0; v < S::TN / 4; v++) {
+            const int cc = c0 + TileMap<S>::col(tx, 4 * v);  // four consecutive columns cc .. cc+3
+            if (vec && cc + 3 < n) {
+                float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (beta != 0.0f) o = *reinterpret_cast<const float4*>(crow + cc);
+                o.x = sgemm_out(alpha, beta, acc[i][4 * v], o.x);
+                o.y = sgemm_out(alpha, beta, acc[i][4 * v + 1], o.y);
+                o.z = sgemm_out(alpha, beta, acc[i][4 * v + 2], o.z);
+                o.w = sgemm_out(alpha, beta, acc[i][4 * v + 3], o.w);
+                *reinterpret_cast<float4*>(crow + cc) = o;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    if (cc + q < n)
+                        crow[cc + q] = sgemm_out(alpha, beta, acc[i][4 * v + q], beta == 0.0f ? 0.0f : crow[cc + q]);
+            }
         }
     }
 }
@@ -86,7 +105,7 @@ int launch_sgemm(int m, int n, int k, float alpha, const float* a, int64_t lda, 
         bb = bt;
         ldb = n;
     }
-    dim3 g((n + 127) / 128, (m + GEMM_RT - 1) / GEMM_RT);
+    dim3 g((n + SgemmTile::BN - 1) / SgemmTile::BN, (m + SgemmTile::BM - 1) / SgemmTile::BM);
     if (a_trans)
         CDCLQ_LAUNCH(sgemm_kernel<true>, g, 256, 0, st, m, n, k, alpha, a, lda, bb, ldb, beta, c, ldc, 0);
     else
@@ -111,7 +130,7 @@ int launch_gram_f32(const float* x, const float* y, int64_t t, int n, double* h,
     const bool sym = (x == y);
     for (int64_t t0 = 0; t0 < t; t0 += TC) {
         int tc = (int)((t - t0) < TC ? (t - t0) : TC);
-        dim3 g((n + 127) / 128, (n + GEMM_RT - 1) / GEMM_RT);
+        dim3 g((n + SgemmTile::BN - 1) / SgemmTile::BN, (n + SgemmTile::BM - 1) / SgemmTile::BM);
         CDCLQ_LAUNCH(sgemm_kernel<true>, g, 256, 0, st, n, n, tc, 1.0f, x + t0 * n, (int64_t)n, y + t0 * n, (int64_t)n,
                      0.0f, tmp, (int64_t)n, sym ? 1 : 0);
         dim3 g2((n + 255) / 256, n);  // n <= 65535 (checked by the caller)

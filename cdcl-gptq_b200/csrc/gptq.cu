@@ -2,7 +2,7 @@
 //
 // One CTA owns up to 64 rows of one layer for the whole pass (rows are independent under the objective,
 // src/engine.rs:9-15).  Per block of B columns:
-//   1. the block w1 = w[:, i1:i2] is staged in shared memory, k-major ([B][65]) so that each row is a column;
+//   1. the block w1 = w[:, i1:i2] is staged in shared memory, k-major ([B][72]) so that each row is a column;
 //   2. columns are processed in order.  Four threads share a row: they compute the group grid together at a
 //      group start (min/max split four ways, the 24 MSE clip candidates split four ways), quantize the
 //      column redundantly, and split the rank-1 in-block compensation w1[:, j+1:i2] -= eps * U[j, j+1:i2]
@@ -18,17 +18,18 @@
 namespace cdclq {
 
 constexpr int P1_ROWS = 64;
+using P1Tile = Tile<P1_ROWS, 128, 16>;  // lazy-update GEMM: 64 rows x 128 columns per step
 // w1 stride: 72 = 8 (mod 32), so the 4 columns x 8 rows a warp touches in one column step fall in 32
 // distinct banks
 constexpr int P1_W1LD = 72;
-constexpr int P1_ELD = GEMM_ALD;  // err1 stride (16-byte aligned k-major A operand)
+constexpr int P1_ELD = P1Tile::ALD;  // err1 stride (16-byte aligned k-major A operand)
 
 static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
 size_t phase1_smem_bytes(int block) {
     size_t b = (size_t)block;
     return align16(b * P1_W1LD * 4) + align16(b * P1_ELD * 4) + align16(b * P1_ROWS) +
-           (size_t)gemm_stage_floats<8>() * 4;
+           (size_t)P1Tile::B_STAGE_FLOATS * 4;
 }
 
 __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __restrict__ items, int B, int mse) {
@@ -156,27 +157,37 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
 
         // ---- lazy update of the columns past the block (src/engine.rs:452-471): w -= err1 * U[i1:i2, i2:]
         if (i2 < n) {
+            using S = P1Tile;
             int ty, tx;
             gemm_coords(tid, ty, tx);
-            for (int c0 = i2; c0 < n; c0 += 128) {
-                float acc[4][8];
+            const bool vec = (n % 4 == 0) && (i2 % 4 == 0);
+            for (int c0 = i2; c0 < n; c0 += S::BN) {
+                float acc[S::TM][S::TN];
 #pragma unroll
-                for (int a = 0; a < 4; a++)
+                for (int a = 0; a < S::TM; a++)
 #pragma unroll
-                    for (int b = 0; b < 8; b++) acc[a][b] = 0.0f;
-                BGlobal<8> Bop{U + (int64_t)i1 * n, (int64_t)n, (int64_t)c0, min(128, n - c0), cnt,
-                               (n % 4 == 0) && (c0 % 4 == 0)};
-                gemm_smem_a<8>(acc, err1, Bop, cnt, stage);
+                    for (int b = 0; b < S::TN; b++) acc[a][b] = 0.0f;
+                BGlobal<S> Bop{U + (int64_t)i1 * n, (int64_t)n, (int64_t)c0, min(S::BN, n - c0), cnt, vec};
+                gemm_smem_a<S>(acc, err1, Bop, cnt, stage);
 #pragma unroll
-                for (int a = 0; a < 4; a++) {
-                    int rr = ty * 4 + a;
+                for (int a = 0; a < S::TM; a++) {
+                    const int rr = TileMap<S>::row(ty, a);
                     if (rr >= rows) continue;
+                    float* wrow = w + (int64_t)rr * n;
 #pragma unroll
-                    for (int b = 0; b < 8; b++) {
-                        int cc = c0 + ColMap<8>::col(tx, b);
-                        if (cc < n) {
-                            float* p = &w[(int64_t)rr * n + cc];
-                            *p = __fsub_rn(*p, acc[a][b]);
+                    for (int v = 0; v < S::TN / 4; v++) {
+                        const int cc = c0 + TileMap<S>::col(tx, 4 * v);  // columns cc .. cc+3
+                        if (vec && cc + 3 < n) {
+                            float4 o = *reinterpret_cast<float4*>(wrow + cc);
+                            o.x = __fsub_rn(o.x, acc[a][4 * v]);
+                            o.y = __fsub_rn(o.y, acc[a][4 * v + 1]);
+                            o.z = __fsub_rn(o.z, acc[a][4 * v + 2]);
+                            o.w = __fsub_rn(o.w, acc[a][4 * v + 3]);
+                            *reinterpret_cast<float4*>(wrow + cc) = o;
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; q++)
+                                if (cc + q < n) wrow[cc + q] = __fsub_rn(wrow[cc + q], acc[a][4 * v + q]);
                         }
                     }
                 }

@@ -119,12 +119,17 @@ int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev,
                        const RepairParams& rp, int g, int sbw, cudaStream_t st);
 int launch_pass_end(const ChunkInfo* chunks_dev, int nchunks, const int* slice_begin_dev, const SliceAcc* acc_dev,
                     const RepairParams& rp, cudaStream_t st);
-size_t repair_smem_bytes(int g, int sbw);
+// Dynamic shared memory of a repair CTA working on tiles of bm (64 or 128) rows.
+size_t repair_smem_bytes(int g, int sbw, int bm);
+// Row-tile height of the persistent repair kernels for chunks of at most max_rows rows: 128 when a chunk has
+// more than 64 rows and two 128-row CTAs fit on one SM, else 64.
+int repair_tile_rows(int g, int sbw, int max_rows);
+constexpr int RP_MAX_TILES_PER_CHUNK = 32;  // mode C keeps at most this many tile partials per chunk
 // All passes + final refit of every chunk in one launch (chunks taken from *counter_dev, in array order).
-int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
                              int* counter_dev, cudaStream_t st);
-// Same with a 2-CTA cluster per chunk (chunks of more than 64 rows, at most 2048 rows).
-int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+// Same with a 2-CTA cluster per chunk (chunks of more than one and at most RP_MAX_TILES_PER_CHUNK tiles).
+int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
                           int* counter_dev, cudaStream_t st);
 
 // ---------------------------------------------------------------------------------------------------------

@@ -3,11 +3,14 @@
 // Work decomposition.  The reference runs phase 2 per row chunk (rc rows): conflict selection sums eps^2
 // over the chunk's rows and the `tol` stop is decided per chunk (src/engine.rs:499-508, 663).  Inside one pass
 // every move (scale refit of a (row, group), code move of a (row, column)) depends only on its own row, so a
-// pass is launched over row SLICES of up to 64 rows; a chunk's slices are reduced in order by a small
-// pass-end kernel that updates the chunk's loss bookkeeping and its stop flag.  Chunks that stopped make
-// every later pass launch a no-op for their slices, which reproduces the per-chunk `break`.
+// chunk's rows are processed in TILES of BM rows (BM = 64 or 128, a compile-time parameter of the kernels)
+// whose per-pass loss deltas are added in tile order.  Three launch modes share the tile code:
+//   A  one launch per pass over 64-row slices, a pass-end kernel reducing each chunk's slices in order (few
+//      chunks: a chunk's rows spread over several SMs);
+//   B  persistent: a CTA takes whole chunks from a counter (heaviest first) and runs all their passes;
+//   C  persistent 2-CTA clusters: the tiles of a chunk of several tiles are split over two SMs.
 //
-// Inside a slice CTA (256 threads):
+// Inside a tile (256 threads):
 //   * the block gradients G = E H[:, c0:c1] run on the FP32 GEMM core (fixed k order, bit-exact);
 //   * the sequential per-row work (refit numerators/denominators, the coordinate sweep with its rank-1
 //     gradient updates) runs one thread per row, in the reference's order, on shared-memory tiles.
@@ -19,10 +22,8 @@
 
 namespace cdclq {
 
-constexpr int RP_ROWS = 64;
-constexpr int RP_LD = 68;  // [col][row] tiles (16-byte aligned rows)
-
 static __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~(size_t)15; }
+
 
 // ---------------------------------------------------------------------------------------------------------
 // Per-chunk statistics after phase 1: colloss (rows summed in order), loss_gptq, sub-block sums, conflict
@@ -92,81 +93,112 @@ int launch_chunk_stats(const ChunkInfo* chunks_dev, int nchunks, const RepairPar
 }
 
 // ---------------------------------------------------------------------------------------------------------
+// GEMM tiles of the repair: result widths 128 (group refit), 64 and 32 (sub-blocks).  A 128-row tile keeps
+// KT = 8 so that two CTAs still fit on one SM.
+template <int BM>
+struct RepairTiles {
+    static constexpr int KT = BM == 128 ? 8 : 16;
+    using W128 = Tile<BM, 128, KT>;
+    using W64 = Tile<BM, 64, KT>;
+    using W32 = Tile<BM, 32, KT>;
+    static constexpr int LD = BM + 4;  // [col][row] result tiles (16-byte aligned rows)
+    static constexpr int STAGE_FLOATS = W128::STAGE_FLOATS > W64::STAGE_FLOATS
+                                            ? (W128::STAGE_FLOATS > W32::STAGE_FLOATS ? W128::STAGE_FLOATS
+                                                                                      : W32::STAGE_FLOATS)
+                                            : (W64::STAGE_FLOATS > W32::STAGE_FLOATS ? W64::STAGE_FLOATS
+                                                                                     : W32::STAGE_FLOATS);
+    static_assert(W128::ALD == LD && W64::ALD == LD && W32::ALD == LD, "result tiles share the A stride");
+};
+
 // A operand of the u H_CC product: A[k][row] = codes[k][row] - z[row] (src/engine.rs:553-558), staged from the
-// shared-memory code tile.
+// shared-memory code tile.  The code tile is k-major ([K][BM] bytes) like the A stage, so a thread converts
+// AP consecutive rows of one k and stores them with one vector store.
+template <class S>
 struct ACodes {
-    const uint8_t* cs;  // [K][RP_ROWS]
-    const float* zr;    // [RP_ROWS]
+    const uint8_t* cs;  // [K][BM]
+    const float* zr;    // [BM]
     int rows_valid;
     int K;
-    __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[4]) const {
-        int row = tid & 63, q = tid >> 6;
-        int k = k0 + q * 4;
+    static constexpr int TPR = S::BM / S::AP;  // threads per k row
+    static_assert(S::AP % 4 == 0, "code rows are converted four at a time");
+    __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[S::AP]) const {
+        const int kr = tid / TPR, c = (tid % TPR) * S::AP, k = k0 + kr;
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-            r[i] = (row < rows_valid && k + i < K) ? __fsub_rn((float)cs[(k + i) * RP_ROWS + row], zr[row]) : 0.0f;
+        for (int v = 0; v < S::AP / 4; v++) {
+            uchar4 q = make_uchar4(0, 0, 0, 0);
+            if (k < K) q = *reinterpret_cast<const uchar4*>(cs + k * S::BM + c + 4 * v);
+            const int b = c + 4 * v;
+            r[4 * v] = (k < K && b < rows_valid) ? __fsub_rn((float)q.x, zr[b]) : 0.0f;
+            r[4 * v + 1] = (k < K && b + 1 < rows_valid) ? __fsub_rn((float)q.y, zr[b + 1]) : 0.0f;
+            r[4 * v + 2] = (k < K && b + 2 < rows_valid) ? __fsub_rn((float)q.z, zr[b + 2]) : 0.0f;
+            r[4 * v + 3] = (k < K && b + 3 < rows_valid) ? __fsub_rn((float)q.w, zr[b + 3]) : 0.0f;
+        }
     }
-    __device__ __forceinline__ void store(float* As, int tid, const float (&r)[4]) const {
-        int row = tid & 63, q = tid >> 6;
+    __device__ __forceinline__ void store(float* As, int tid, const float (&r)[S::AP]) const {
+        const int kr = tid / TPR, c = (tid % TPR) * S::AP;
 #pragma unroll
-        for (int i = 0; i < 4; i++) As[(q * 4 + i) * GEMM_ALD + row] = r[i];
+        for (int v = 0; v < S::AP / 4; v++)
+            *reinterpret_cast<float4*>(As + kr * S::ALD + c + 4 * v) =
+                make_float4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
     }
 };
 
-// out[c][row] = (A B)[row][c] for c < wd (wd <= 128), via the widest fitting tile.  Ends synchronised.
-template <class AL>
-__device__ void gemm_to_tile(const AL& A, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
-                             float* stage) {
-    const int tid = threadIdx.x;
+// The A operand of a repair GEMM: the error rows E (global) or the centred codes (shared memory).
+struct AFromE {
+    const float* e;
+    int64_t lde;
+    int rows_valid;
+    int K;
+    bool vec;
+    template <class S>
+    __device__ __forceinline__ AGlobal<S> make() const { return AGlobal<S>{e, lde, rows_valid, K, vec}; }
+};
+struct AFromCodes {
+    const uint8_t* cs;
+    const float* zr;
+    int rows_valid;
+    int K;
+    template <class S>
+    __device__ __forceinline__ ACodes<S> make() const { return ACodes<S>{cs, zr, rows_valid, K}; }
+};
+
+template <class S, class AM>
+__device__ __forceinline__ void gemm_to_tile_s(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd,
+                                               int K, float* out, float* stage) {
     int ty, tx;
-    gemm_coords(tid, ty, tx);
-    const bool vec = (ldb % 4 == 0) && (col0 % 4 == 0);
-    if (wd > 64) {
-        float acc[4][8];
+    gemm_coords(threadIdx.x, ty, tx);
+    float acc[S::TM][S::TN];
 #pragma unroll
-        for (int a = 0; a < 4; a++)
+    for (int i = 0; i < S::TM; i++)
 #pragma unroll
-            for (int c = 0; c < 8; c++) acc[a][c] = 0.0f;
-        BGlobal<8> Bop{b, ldb, col0, wd, K, vec};
-        gemm_loader_a<8>(acc, A, Bop, K, stage);
+        for (int j = 0; j < S::TN; j++) acc[i][j] = 0.0f;
+    const auto A = am.template make<S>();
+    BGlobal<S> Bop{b, ldb, col0, wd, K, (ldb % 4 == 0) && (col0 % 4 == 0)};
+    gemm_loader_a<S>(acc, A, Bop, K, stage);
 #pragma unroll
-        for (int a = 0; a < 4; a++)
+    for (int j = 0; j < S::TN; j++) {
+        const int cc = TileMap<S>::col(tx, j);
+        if (cc < wd) {
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                int cc = ColMap<8>::col(tx, c);
-                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
-            }
-    } else if (wd > 32) {
-        float acc[4][4];
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < 4; c++) acc[a][c] = 0.0f;
-        BGlobal<4> Bop{b, ldb, col0, wd, K, vec};
-        gemm_loader_a<4>(acc, A, Bop, K, stage);
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                int cc = ColMap<4>::col(tx, c);
-                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
-            }
-    } else {
-        float acc[4][2];
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < 2; c++) acc[a][c] = 0.0f;
-        BGlobal<2> Bop{b, ldb, col0, wd, K, false};
-        gemm_loader_a<2>(acc, A, Bop, K, stage);
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int c = 0; c < 2; c++) {
-                int cc = ColMap<2>::col(tx, c);
-                if (cc < wd) out[cc * RP_LD + ty * 4 + a] = acc[a][c];
-            }
+            for (int v = 0; v < S::TM / 4; v++)
+                *reinterpret_cast<float4*>(out + cc * S::ALD + TileMap<S>::row(ty, 4 * v)) =
+                    make_float4(acc[4 * v][j], acc[4 * v + 1][j], acc[4 * v + 2][j], acc[4 * v + 3][j]);
+        }
     }
+}
+
+// out[c][row] = (A B)[row][c] for c < wd (wd <= 128), B = b[k][col0 + c], via the narrowest fitting tile.
+// Ends synchronised.
+template <int BM, class AM>
+__device__ void gemm_to_tile(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
+                             float* stage) {
+    using RT = RepairTiles<BM>;
+    if (wd > 64)
+        gemm_to_tile_s<typename RT::W128>(am, b, ldb, col0, wd, K, out, stage);
+    else if (wd > 32)
+        gemm_to_tile_s<typename RT::W64>(am, b, ldb, col0, wd, K, out, stage);
+    else
+        gemm_to_tile_s<typename RT::W32>(am, b, ldb, col0, wd, K, out, stage);
     __syncthreads();
 }
 
@@ -184,23 +216,27 @@ static __host__ __device__ inline size_t cd_hss_bytes(int sbw) {
     return full <= (size_t)HSS_MAX_BYTES ? al16(full) : al16((size_t)sbw * 4);
 }
 
+template <int BM>
 static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
+    constexpr int LD = RepairTiles<BM>::LD;
     RepairLayout L;
     size_t gcap = (size_t)(g < 1024 ? g : 1024);
-    size_t refit = al16(gcap * RP_ROWS) + al16((size_t)128 * RP_LD * 4);
-    size_t cd = al16((size_t)sbw * RP_ROWS) + 2 * al16((size_t)sbw * RP_LD * 4) + cd_hss_bytes(sbw);
+    size_t refit = al16(gcap * BM) + al16((size_t)128 * LD * 4);
+    size_t cd = al16((size_t)sbw * BM) + 2 * al16((size_t)sbw * LD * 4) + cd_hss_bytes(sbw);
     L.body = refit > cd ? refit : cd;
     L.zrow = L.body;
-    L.snew = L.zrow + RP_ROWS * 4;
-    L.accept = L.snew + RP_ROWS * 4;
-    L.rowdelta = L.accept + RP_ROWS * 4;
-    L.upd = L.rowdelta + RP_ROWS * 8;
-    L.stage = L.upd + RP_ROWS * 8;
-    L.total = L.stage + (size_t)gemm_stage_floats<8>() * 4;
+    L.snew = L.zrow + BM * 4;
+    L.accept = L.snew + BM * 4;
+    L.rowdelta = L.accept + BM * 4;
+    L.upd = L.rowdelta + BM * 8;
+    L.stage = L.upd + BM * 8;
+    L.total = L.stage + (size_t)RepairTiles<BM>::STAGE_FLOATS * 4;
     return L;
 }
 
-size_t repair_smem_bytes(int g, int sbw) { return repair_layout(g, sbw).total; }
+size_t repair_smem_bytes(int g, int sbw, int bm) {
+    return bm == 128 ? repair_layout<128>(g, sbw).total : repair_layout<64>(g, sbw).total;
+}
 
 struct TileSmem {
     unsigned char* body;
@@ -212,8 +248,9 @@ struct TileSmem {
     float* stage;
 };
 
+template <int BM>
 __device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw) {
-    const RepairLayout L = repair_layout(g, sbw);
+    const RepairLayout L = repair_layout<BM>(g, sbw);
     TileSmem t;
     t.body = raw;
     t.zrow = reinterpret_cast<float*>(raw + L.zrow);
@@ -228,8 +265,10 @@ __device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw
 // ---------------------------------------------------------------------------------------------------------
 // Closed-form scale refit of every (row, group) of the rows [r0, r0 + rs) of a chunk, groups in order
 // (src/engine.rs:534-589).  Thread r < rs accumulates its row's accepted loss deltas and refits.
+template <int BM>
 __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& sm, double& my_delta,
                            unsigned long long& my_upd) {
+    constexpr int LD = RepairTiles<BM>::LD;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng;
     const size_t gcap = (size_t)(g < 1024 ? g : 1024);
     float* E = ci.e + (int64_t)r0 * n;
@@ -238,27 +277,27 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
     float* SC = ci.scales + (int64_t)r0 * ng;
     const float* ZR = ci.zeros + (int64_t)r0 * ng;
     const float* H = ci.h;
-    uint8_t* cs = sm.body;                                                   // [gcap][64] codes of the group
-    float* tile = reinterpret_cast<float*>(sm.body + al16(gcap * RP_ROWS));  // [128][68] G, then u H_CC
+    uint8_t* cs = sm.body;                                              // [gcap][BM] codes of the group
+    float* tile = reinterpret_cast<float*>(sm.body + al16(gcap * BM));  // [128][LD] G, then u H_CC
     for (int gi = 0; gi < ng; gi++) {
         const int c0 = gi * g, wd = min(g, n - c0);
         for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
-            cs[k * RP_ROWS + rr] = CODES[(int64_t)rr * n + c0 + k];
+            cs[k * BM + rr] = CODES[(int64_t)rr * n + c0 + k];
         }
-        if (tid < RP_ROWS) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
+        if (tid < BM) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
         __syncthreads();
         // num = sum_k u_k * G_k with G = E H[:, c0:c1]
         float num = 0.0f, den = 0.0f;
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
-            gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, tile, sm.stage);
+            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                             tile, sm.stage);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
-                    float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
-                    num = __fadd_rn(num, __fmul_rn(u, tile[k * RP_LD + tid]));
+                    float u = __fsub_rn((float)cs[(t0 + k) * BM + tid], zr);
+                    num = __fadd_rn(num, __fmul_rn(u, tile[k * LD + tid]));
                 }
             }
             __syncthreads();
@@ -266,18 +305,18 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         // den = sum_k u_k * (u H_CC)_k
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            ACodes A{cs, sm.zrow, rs, wd};
-            gemm_to_tile(A, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0), wt, wd, tile, sm.stage);
+            gemm_to_tile<BM>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
+                             wt, wd, tile, sm.stage);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
-                    float u = __fsub_rn((float)cs[(t0 + k) * RP_ROWS + tid], zr);
-                    den = __fadd_rn(den, __fmul_rn(u, tile[k * RP_LD + tid]));
+                    float u = __fsub_rn((float)cs[(t0 + k) * BM + tid], zr);
+                    den = __fadd_rn(den, __fmul_rn(u, tile[k * LD + tid]));
                 }
             }
             __syncthreads();
         }
-        if (tid < RP_ROWS) sm.accept[tid] = 0;
+        if (tid < BM) sm.accept[tid] = 0;
         if (tid < rs && den > 1e-30f) {
             const float s_old = SC[(int64_t)tid * ng + gi];
             float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
@@ -297,7 +336,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
             if (sm.accept[rr]) {
-                float u = __fsub_rn((float)cs[k * RP_ROWS + rr], sm.zrow[rr]);
+                float u = __fsub_rn((float)cs[k * BM + rr], sm.zrow[rr]);
                 float ndq = __fmul_rn(sm.snew[rr], u);
                 int64_t off = (int64_t)rr * n + c0 + k;
                 E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
@@ -309,8 +348,10 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
 }
 
 // Coordinate descent over the selected sub-blocks for rows [r0, r0 + rs) (src/engine.rs:600-658).
+template <int BM>
 __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
                         unsigned long long& my_upd) {
+    constexpr int LD = RepairTiles<BM>::LD;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
     float* E = ci.e + (int64_t)r0 * n;
     float* WQ = ci.wq + (int64_t)r0 * n;
@@ -319,10 +360,10 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
     const float* ZR = ci.zeros + (int64_t)r0 * ng;
     const float* H = ci.h;
     const int n_sel = ci.st->n_sel;
-    uint8_t* cs = sm.body;                                                      // [sbw][64]
-    float* gt = reinterpret_cast<float*>(sm.body + al16((size_t)sbw * RP_ROWS));  // [sbw][68] block gradient
-    float* wqs = gt + (size_t)sbw * RP_LD;                                      // [sbw][68] W_hat
-    float* hss = wqs + (size_t)sbw * RP_LD;                                     // [sbw][sbw] or its diagonal
+    uint8_t* cs = sm.body;                                                 // [sbw][BM]
+    float* gt = reinterpret_cast<float*>(sm.body + al16((size_t)sbw * BM));  // [sbw][LD] block gradient
+    float* wqs = gt + (size_t)sbw * LD;                                    // [sbw][LD] W_hat
+    float* hss = wqs + (size_t)sbw * LD;                                   // [sbw][sbw] or its diagonal
     const bool hss_full = (size_t)sbw * sbw * 4 <= (size_t)HSS_MAX_BYTES;
     for (int si = 0; si < n_sel; si++) {
         const int s = ci.sel[si];
@@ -330,8 +371,8 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
             int64_t off = (int64_t)rr * n + c0 + k;
-            cs[k * RP_ROWS + rr] = CODES[off];
-            wqs[k * RP_LD + rr] = WQ[off];
+            cs[k * BM + rr] = CODES[off];
+            wqs[k * LD + rr] = WQ[off];
         }
         if (hss_full) {
             for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
@@ -343,8 +384,8 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         }
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            AGlobal A{E, (int64_t)n, rs, n, (n % 4 == 0)};
-            gemm_to_tile(A, H, (int64_t)n, (int64_t)(c0 + t0), wt, n, gt + (size_t)t0 * RP_LD, sm.stage);
+            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                             gt + (size_t)t0 * LD, sm.stage);
         }
         if (tid < rs) {
             const int r = tid;
@@ -362,15 +403,15 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                         z = ZR[(int64_t)r * ng + gi];
                     }
                     const float hjj = hss_full ? hss[jj * wd + jj] : hss[jj];
-                    const float cur = wqs[jj * RP_LD + r];
-                    const float gj = gt[jj * RP_LD + r];
+                    const float cur = wqs[jj * LD + r];
+                    const float gj = gt[jj * LD + r];
                     const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
                     float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
                     if (q < 0.0f) q = 0.0f;
                     if (q > maxq) q = maxq;
                     const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
                     const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
-                    if (qc != cs[jj * RP_ROWS + r]) {
+                    if (qc != cs[jj * BM + r]) {
                         // closed-form loss change, then the rank-1 gradient update (src/engine.rs:634-650)
                         const float de = __fsub_rn(cur, newdq);
                         const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
@@ -379,18 +420,18 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                         if (hss_full) {
                             const float* hrow = hss + jj * wd;
                             for (int kk = 0; kk < wd; kk++) {
-                                float* gp = &gt[kk * RP_LD + r];
+                                float* gp = &gt[kk * LD + r];
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, hrow[kk]));
                             }
                         } else {
                             const float* hrow = H + (int64_t)j * n + c0;
                             for (int kk = 0; kk < wd; kk++) {
-                                float* gp = &gt[kk * RP_LD + r];
+                                float* gp = &gt[kk * LD + r];
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
                             }
                         }
-                        wqs[jj * RP_LD + r] = newdq;
-                        cs[jj * RP_ROWS + r] = qc;
+                        wqs[jj * LD + r] = newdq;
+                        cs[jj * BM + r] = qc;
                         float* ep = &E[(int64_t)r * n + j];
                         *ep = __fadd_rn(*ep, de);
                         my_upd++;
@@ -404,19 +445,20 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
             int64_t off = (int64_t)rr * n + c0 + k;
-            CODES[off] = cs[k * RP_ROWS + rr];
-            WQ[off] = wqs[k * RP_LD + rr];
+            CODES[off] = cs[k * BM + rr];
+            WQ[off] = wqs[k * LD + rr];
         }
         __syncthreads();
     }
 }
 
 // Sum of the tile's per-row results, rows in order; valid in thread 0.  Ends synchronised.
+template <int BM>
 __device__ __forceinline__ void tile_reduce(int rs, const TileSmem& sm, double my_delta, unsigned long long my_upd,
                                             double& d, unsigned long long& u) {
     const int tid = threadIdx.x;
     __syncthreads();
-    if (tid < RP_ROWS) {
+    if (tid < BM) {
         sm.rowdelta[tid] = (tid < rs) ? my_delta : 0.0;
         sm.rowupd[tid] = (tid < rs) ? my_upd : 0ull;
     }
@@ -430,6 +472,18 @@ __device__ __forceinline__ void tile_reduce(int rs, const TileSmem& sm, double m
         }
     }
     __syncthreads();
+}
+
+// One tile of one pass (refit then coordinate descent, or the final refit alone); the tile's delta and
+// update count are valid in thread 0.
+template <int BM>
+__device__ __forceinline__ void run_tile(const ChunkInfo& ci, int r0, int rs, const RepairParams& rp, bool final_refit,
+                                         const TileSmem& sm, double& d, unsigned long long& u) {
+    double my_delta = 0.0;
+    unsigned long long my_upd = 0ull;
+    if (rp.do_refit) refit_tile<BM>(ci, r0, rs, sm, my_delta, my_upd);
+    if (rp.do_cd && !final_refit) cd_tile<BM>(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+    tile_reduce<BM>(rs, sm, my_delta, my_upd, d, u);
 }
 
 // The reference's stop rule after a pass (src/engine.rs:660-665), in thread 0 / one thread.
@@ -454,14 +508,10 @@ __global__ void __launch_bounds__(256, 2) repair_pass_kernel(const ChunkInfo* __
     if (threadIdx.x == 0) ci = chunks[sl.chunk];
     __syncthreads();
     if (!rp.final_refit && ci.st->done) return;  // this chunk has converged (src/engine.rs:663-665)
-    const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
-    double my_delta = 0.0;
-    unsigned long long my_upd = 0ull;
-    if (rp.do_refit) refit_tile(ci, sl.r0, sl.rs, sm, my_delta, my_upd);
-    if (rp.do_cd && !rp.final_refit) cd_tile(ci, sl.r0, sl.rs, rp.cd_sweeps, sm, my_delta, my_upd);
+    const TileSmem sm = tile_smem<64>(smem_raw, ci.g, ci.sbw);
     double d;
     unsigned long long u;
-    tile_reduce(sl.rs, sm, my_delta, my_upd, d, u);
+    run_tile<64>(ci, sl.r0, sl.rs, rp, rp.final_refit != 0, sm, d, u);
     if (threadIdx.x == 0) {
         acc_out[blockIdx.x].delta = d;
         acc_out[blockIdx.x].updates = u;
@@ -470,7 +520,8 @@ __global__ void __launch_bounds__(256, 2) repair_pass_kernel(const ChunkInfo* __
 
 // Mode B - persistent: each CTA takes whole row chunks from a counter (heaviest first) and runs all of a
 // chunk's passes, its stop rule and its final refit itself, so no launch-wide barrier separates passes.  The
-// arithmetic and every reduction order are those of mode A (tiles of 64 rows = mode A's slices).
+// arithmetic is that of mode A; the pass delta adds the BM-row tiles' sums in tile order.
+template <int BM>
 __global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkInfo* __restrict__ chunks, int nchunks,
                                                                    RepairParams rp, int* __restrict__ counter) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -486,21 +537,16 @@ __global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkIn
         const int c = s_chunk;
         if (c >= nchunks) return;
         ChunkState* st = ci.st;
-        const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
+        const TileSmem sm = tile_smem<BM>(smem_raw, ci.g, ci.sbw);
         if (tid == 0) s_done = st->done;
         __syncthreads();
         for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
             double pd = 0.0;
             unsigned long long pu = 0ull;
-            for (int r0 = 0; r0 < ci.rows; r0 += RP_ROWS) {
-                const int rs = min(RP_ROWS, ci.rows - r0);
-                double my_delta = 0.0;
-                unsigned long long my_upd = 0ull;
-                if (rp.do_refit) refit_tile(ci, r0, rs, sm, my_delta, my_upd);
-                if (rp.do_cd) cd_tile(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+            for (int r0 = 0; r0 < ci.rows; r0 += BM) {
                 double d;
                 unsigned long long u;
-                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, false, sm, d, u);
                 if (tid == 0) {
                     pd = __dadd_rn(pd, d);
                     pu += u;
@@ -515,14 +561,10 @@ __global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkIn
         if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
             double fd = 0.0;
             unsigned long long fu = 0ull;
-            for (int r0 = 0; r0 < ci.rows; r0 += RP_ROWS) {
-                const int rs = min(RP_ROWS, ci.rows - r0);
-                double my_delta = 0.0;
-                unsigned long long my_upd = 0ull;
-                refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+            for (int r0 = 0; r0 < ci.rows; r0 += BM) {
                 double d;
                 unsigned long long u;
-                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, true, sm, d, u);
                 if (tid == 0) {
                     fd = __dadd_rn(fd, d);
                     fu += u;
@@ -537,14 +579,15 @@ __global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkIn
     }
 }
 
-// Mode C - persistent clusters: a cluster of 2 CTAs takes a whole row chunk (heaviest first); CTA rank r
-// handles the chunk's 64-row tiles r, r+2, ...  A row chunk's passes are the latency-critical unit (a
-// 128-row down_proj chunk does 7.5x the work of a 2048-wide one), and splitting its rows over two SMs halves
-// that critical path.  At the end of each pass the tiles' partial sums are written into rank 0's shared
-// memory (distributed shared memory), rank 0 adds them in tile order - the order of modes A and B - applies
-// the stop rule and writes the decision back into rank 1; hardware cluster barriers order these steps.
-constexpr int RP_MAX_TILES = 32;  // chunks up to 2048 rows
+// Mode C - persistent clusters: a cluster of 2 CTAs takes a whole row chunk of several tiles (heaviest first);
+// CTA rank r handles the chunk's tiles r, r+2, ...  A row chunk's passes are the latency-critical unit, and
+// splitting its rows over two SMs halves that critical path.  At the end of each pass the tiles' partial sums
+// are written into rank 0's shared memory (distributed shared memory), rank 0 adds them in tile order - the
+// order of mode B - applies the stop rule and writes the decision back into rank 1; hardware cluster barriers
+// order these steps.
+constexpr int RP_MAX_TILES = RP_MAX_TILES_PER_CHUNK;
 
+template <int BM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
     repair_cluster_kernel(const ChunkInfo* __restrict__ chunks, int nchunks, RepairParams rp, int* __restrict__ counter) {
     namespace cg = cooperative_groups;
@@ -568,20 +611,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
         cluster.sync();  // every rank has read rank 0's s_chunk before anyone may leave or overwrite it
         if (c >= nchunks) return;
         ChunkState* st = ci.st;
-        const TileSmem sm = tile_smem(smem_raw, ci.g, ci.sbw);
-        const int ntiles = (ci.rows + RP_ROWS - 1) / RP_ROWS;
+        const TileSmem sm = tile_smem<BM>(smem_raw, ci.g, ci.sbw);
+        const int ntiles = (ci.rows + BM - 1) / BM;
         if (tid == 0) s_done = st->done;
         __syncthreads();
         for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
             for (int t = rank; t < ntiles; t += 2) {
-                const int r0 = t * RP_ROWS, rs = min(RP_ROWS, ci.rows - r0);
-                double my_delta = 0.0;
-                unsigned long long my_upd = 0ull;
-                if (rp.do_refit) refit_tile(ci, r0, rs, sm, my_delta, my_upd);
-                if (rp.do_cd) cd_tile(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+                const int r0 = t * BM;
                 double d;
                 unsigned long long u;
-                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, false, sm, d, u);
                 if (tid == 0) {
                     tdelta0[t] = d;
                     tupd0[t] = u;
@@ -603,13 +642,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
         }
         if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
             for (int t = rank; t < ntiles; t += 2) {
-                const int r0 = t * RP_ROWS, rs = min(RP_ROWS, ci.rows - r0);
-                double my_delta = 0.0;
-                unsigned long long my_upd = 0ull;
-                refit_tile(ci, r0, rs, sm, my_delta, my_upd);
+                const int r0 = t * BM;
                 double d;
                 unsigned long long u;
-                tile_reduce(rs, sm, my_delta, my_upd, d, u);
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, true, sm, d, u);
                 if (tid == 0) {
                     tdelta0[t] = d;
                     tupd0[t] = u;
@@ -636,10 +672,33 @@ static int set_repair_smem(const void* fn, size_t smem) {
     return e == cudaSuccess ? 0 : cuda_error(e, "repair smem attribute");
 }
 
+static int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+int repair_tile_rows(int g, int sbw, int max_rows) {
+    if (max_rows <= 64) return 64;
+    // 128-row tiles only while two CTAs still fit on one SM
+    const size_t smem = repair_smem_bytes(g, sbw, 128);
+    if (set_repair_smem((const void*)repair_persistent_kernel<128>, smem)) {
+        cudaGetLastError();
+        return 64;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel<128>, 256, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 64;
+    }
+    return per_sm >= 2 ? 128 : 64;
+}
+
 int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev, int nslices, SliceAcc* acc_dev,
                        const RepairParams& rp, int g, int sbw, cudaStream_t st) {
     if (nslices == 0) return 0;
-    size_t smem = repair_smem_bytes(g, sbw);
+    size_t smem = repair_smem_bytes(g, sbw, 64);
     int rc = set_repair_smem((const void*)repair_pass_kernel, smem);
     if (rc) return rc;
     CDCLQ_LAUNCH(repair_pass_kernel, nslices, 256, smem, st, chunks_dev, slices_dev, acc_dev, rp);
@@ -647,43 +706,53 @@ int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev,
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_pass_kernel launch");
 }
 
-int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
-                          int* counter_dev, cudaStream_t st) {
-    if (nchunks == 0) return 0;
-    size_t smem = repair_smem_bytes(g, sbw);
-    int rc = set_repair_smem((const void*)repair_cluster_kernel, smem);
+template <int BM>
+static int launch_cluster_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                             int* counter_dev, cudaStream_t st) {
+    int rc = set_repair_smem((const void*)repair_cluster_kernel<BM>, smem);
     if (rc) return rc;
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_cluster_kernel, 256, smem);
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_cluster_kernel<BM>, 256, smem);
     if (per_sm < 1) per_sm = 1;
-    int clusters = sms * per_sm / 2;
+    int clusters = sm_count() * per_sm / 2;
     if (clusters > nchunks) clusters = nchunks;
     if (clusters < 1) clusters = 1;
     CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
-    CDCLQ_LAUNCH(repair_cluster_kernel, 2 * clusters, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    CDCLQ_LAUNCH(repair_cluster_kernel<BM>, 2 * clusters, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_cluster_kernel launch");
 }
 
-int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
-                             int* counter_dev, cudaStream_t st) {
+int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
+                          int* counter_dev, cudaStream_t st) {
     if (nchunks == 0) return 0;
-    size_t smem = repair_smem_bytes(g, sbw);
-    int rc = set_repair_smem((const void*)repair_persistent_kernel, smem);
+    size_t smem = repair_smem_bytes(g, sbw, bm);
+    return bm == 128 ? launch_cluster_bm<128>(chunks_dev, nchunks, rp, smem, counter_dev, st)
+                     : launch_cluster_bm<64>(chunks_dev, nchunks, rp, smem, counter_dev, st);
+}
+
+template <int BM>
+static int launch_persistent_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                                int* counter_dev, cudaStream_t st) {
+    int rc = set_repair_smem((const void*)repair_persistent_kernel<BM>, smem);
     if (rc) return rc;
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel, 256, smem);
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel<BM>, 256, smem);
     if (per_sm < 1) per_sm = 1;
-    int grid = sms * per_sm;
+    int grid = sm_count() * per_sm;
     if (grid > nchunks) grid = nchunks;
     CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
-    CDCLQ_LAUNCH(repair_persistent_kernel, grid, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    CDCLQ_LAUNCH(repair_persistent_kernel<BM>, grid, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_persistent_kernel launch");
+}
+
+int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
+                             int* counter_dev, cudaStream_t st) {
+    if (nchunks == 0) return 0;
+    size_t smem = repair_smem_bytes(g, sbw, bm);
+    return bm == 128 ? launch_persistent_bm<128>(chunks_dev, nchunks, rp, smem, counter_dev, st)
+                     : launch_persistent_bm<64>(chunks_dev, nchunks, rp, smem, counter_dev, st);
 }
 
 // ---------------------------------------------------------------------------------------------------------
