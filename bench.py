@@ -477,7 +477,8 @@ def main():
                                                            "ms_final")}},
             "gpu_launches": int(launches),
             "roofline": {
-                "kernel": "repair_pass_kernel (CDCL repair gradients on the FP32 SIMT GEMM core)",
+                "kernel": "repair_persistent_kernel (CDCL repair: block gradients on the FP32 SIMT GEMM core, "
+                          "per-row refit and coordinate descent)",
                 "bound": "fp32", "achieved": rep_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": rep_tflops / fp32_peak if fp32_peak else None, "traffic": None,
                 "peak_source": "measured in this run: cuBLAS SGEMM 8192^3 with TF32 off (FFMA); MEASURED_PEAKS.json "

@@ -12,7 +12,8 @@
 // the groups spaced BN/(TN/4) apart (TN = 2: two adjacent columns).  Each warp covers 8 (tx) x 4 (ty) threads,
 // so a k-step's fragment loads are single 128-byte shared-memory wavefronts.  K is consumed in stages of KT:
 // the A stage is held k-major in shared memory ([KT][BM+4], one 16-byte load = 4 rows of a thread), the B stage
-// row-major ([KT][BN]); the next stage is fetched into registers while the current one is multiplied.
+// row-major ([KT][BN]); the next stage is fetched into registers while the current one is multiplied, and
+// within a stage the fragments of the next k-step are read while the current k-step's products issue.
 #pragma once
 
 #include <cstdint>
@@ -52,34 +53,42 @@ struct TileMap {
     }
 };
 
-// Multiply-accumulate one KT stage held in shared memory (the first kn k-steps of it).
+// Multiply-accumulate one KT stage held in shared memory (the first kn k-steps of it); the fragments of k-step
+// kk+1 are loaded before the products of kk are issued.
+template <class S>
+__device__ __forceinline__ void frag_load(float (&av)[S::TM], float (&bv)[S::TN], const float* __restrict__ As,
+                                          const float* __restrict__ Bs, int kk, int ty, int tx) {
+#pragma unroll
+    for (int v = 0; v < S::TM / 4; v++) {
+        float4 a = *reinterpret_cast<const float4*>(As + kk * S::ALD + ty * S::TM + 4 * v);
+        av[4 * v] = a.x; av[4 * v + 1] = a.y; av[4 * v + 2] = a.z; av[4 * v + 3] = a.w;
+    }
+    const float* brow = Bs + kk * S::BN;
+    if constexpr (S::TN == 2) {
+        float2 b = *reinterpret_cast<const float2*>(brow + tx * 2);
+        bv[0] = b.x; bv[1] = b.y;
+    } else {
+#pragma unroll
+        for (int v = 0; v < S::TN / 4; v++) {
+            float4 b = *reinterpret_cast<const float4*>(brow + v * (S::BN / (S::TN / 4)) + tx * 4);
+            bv[4 * v] = b.x; bv[4 * v + 1] = b.y; bv[4 * v + 2] = b.z; bv[4 * v + 3] = b.w;
+        }
+    }
+}
+
 template <class S>
 __device__ __forceinline__ void gemm_stage_mac(float (&acc)[S::TM][S::TN], const float* __restrict__ As,
                                                const float* __restrict__ Bs, int ty, int tx, int kn = S::KT) {
+    float av[2][S::TM], bv[2][S::TN];
+    frag_load<S>(av[0], bv[0], As, Bs, 0, ty, tx);
 #pragma unroll
     for (int kk = 0; kk < S::KT; kk++) {
+        if (kk + 1 < S::KT && kk + 1 < kn) frag_load<S>(av[(kk + 1) & 1], bv[(kk + 1) & 1], As, Bs, kk + 1, ty, tx);
         if (kk < kn) {
-            float av[S::TM], bv[S::TN];
-#pragma unroll
-            for (int v = 0; v < S::TM / 4; v++) {
-                float4 a = *reinterpret_cast<const float4*>(As + kk * S::ALD + ty * S::TM + 4 * v);
-                av[4 * v] = a.x; av[4 * v + 1] = a.y; av[4 * v + 2] = a.z; av[4 * v + 3] = a.w;
-            }
-            const float* brow = Bs + kk * S::BN;
-            if constexpr (S::TN == 2) {
-                float2 b = *reinterpret_cast<const float2*>(brow + tx * 2);
-                bv[0] = b.x; bv[1] = b.y;
-            } else {
-#pragma unroll
-                for (int v = 0; v < S::TN / 4; v++) {
-                    float4 b = *reinterpret_cast<const float4*>(brow + v * (S::BN / (S::TN / 4)) + tx * 4);
-                    bv[4 * v] = b.x; bv[4 * v + 1] = b.y; bv[4 * v + 2] = b.z; bv[4 * v + 3] = b.w;
-                }
-            }
 #pragma unroll
             for (int i = 0; i < S::TM; i++)
 #pragma unroll
-                for (int j = 0; j < S::TN; j++) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < S::TN; j++) acc[i][j] = __fmaf_rn(av[kk & 1][i], bv[kk & 1][j], acc[i][j]);
         }
     }
 }

@@ -93,15 +93,18 @@ int launch_chunk_stats(const ChunkInfo* chunks_dev, int nchunks, const RepairPar
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// GEMM tiles of the repair: result widths 128 (group refit), 64 and 32 (sub-blocks).  A 128-row tile keeps
-// KT = 8 so that two CTAs still fit on one SM.
+// GEMM tiles of the repair: result widths 128 (group refit), 64 and 32 (sub-blocks), K stages of 16.  The
+// staging buffers of a GEMM share shared memory with the tile that receives its result (the result is only
+// written after the last stage has been consumed), which keeps two 128-row CTAs on one SM.
 template <int BM>
 struct RepairTiles {
-    static constexpr int KT = BM == 128 ? 8 : 16;
+    static constexpr int KT = 16;
     using W128 = Tile<BM, 128, KT>;
     using W64 = Tile<BM, 64, KT>;
     using W32 = Tile<BM, 32, KT>;
-    static constexpr int LD = BM + 4;  // [col][row] result tiles (16-byte aligned rows)
+    static constexpr int LD = BM + 4;    // [col][row] GEMM result tiles (16-byte aligned rows)
+    static constexpr int CSLD = BM + 4;  // [col][row] code tiles, bytes: consecutive columns start in distinct banks
+    static constexpr int LDW = BM + 1;   // [col][row] W_hat tile: consecutive columns start in distinct banks
     static constexpr int STAGE_FLOATS = W128::STAGE_FLOATS > W64::STAGE_FLOATS
                                             ? (W128::STAGE_FLOATS > W32::STAGE_FLOATS ? W128::STAGE_FLOATS
                                                                                       : W32::STAGE_FLOATS)
@@ -115,23 +118,25 @@ struct RepairTiles {
 // AP consecutive rows of one k and stores them with one vector store.
 template <class S>
 struct ACodes {
-    const uint8_t* cs;  // [K][BM]
-    const float* zr;    // [BM]
+    const uint8_t* cs;  // [K][BM + 4]
+    const float* zr;    // [BM], 16-byte aligned
     int rows_valid;
     int K;
     static constexpr int TPR = S::BM / S::AP;  // threads per k row
+    static constexpr int LDC = S::BM + 4;
     static_assert(S::AP % 4 == 0, "code rows are converted four at a time");
     __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[S::AP]) const {
         const int kr = tid / TPR, c = (tid % TPR) * S::AP, k = k0 + kr;
 #pragma unroll
         for (int v = 0; v < S::AP / 4; v++) {
             uchar4 q = make_uchar4(0, 0, 0, 0);
-            if (k < K) q = *reinterpret_cast<const uchar4*>(cs + k * S::BM + c + 4 * v);
+            if (k < K) q = *reinterpret_cast<const uchar4*>(cs + k * LDC + c + 4 * v);
             const int b = c + 4 * v;
-            r[4 * v] = (k < K && b < rows_valid) ? __fsub_rn((float)q.x, zr[b]) : 0.0f;
-            r[4 * v + 1] = (k < K && b + 1 < rows_valid) ? __fsub_rn((float)q.y, zr[b + 1]) : 0.0f;
-            r[4 * v + 2] = (k < K && b + 2 < rows_valid) ? __fsub_rn((float)q.z, zr[b + 2]) : 0.0f;
-            r[4 * v + 3] = (k < K && b + 3 < rows_valid) ? __fsub_rn((float)q.w, zr[b + 3]) : 0.0f;
+            const float4 z = *reinterpret_cast<const float4*>(zr + b);
+            r[4 * v] = (k < K && b < rows_valid) ? __fsub_rn((float)q.x, z.x) : 0.0f;
+            r[4 * v + 1] = (k < K && b + 1 < rows_valid) ? __fsub_rn((float)q.y, z.y) : 0.0f;
+            r[4 * v + 2] = (k < K && b + 2 < rows_valid) ? __fsub_rn((float)q.z, z.z) : 0.0f;
+            r[4 * v + 3] = (k < K && b + 3 < rows_valid) ? __fsub_rn((float)q.w, z.w) : 0.0f;
         }
     }
     __device__ __forceinline__ void store(float* As, int tid, const float (&r)[S::AP]) const {
@@ -202,13 +207,71 @@ __device__ void gemm_to_tile(const AM& am, const float* b, int64_t ldb, int64_t 
     __syncthreads();
 }
 
+// Tile staging between the row-major global matrices and the [col][row] shared-memory tiles.  A thread moves
+// one column of four consecutive rows: its global accesses are coalesced across the warp (consecutive
+// columns), and its shared-memory word lands in a distinct bank per column (strides CSLD / LDW).
+template <int BM>
+__device__ __forceinline__ void stage_codes(uint8_t* cs, const uint8_t* codes, int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if (r + i < rs) word |= (uint32_t)codes[(int64_t)(r + i) * n + c0 + k] << (8 * i);
+        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+    }
+}
+
+template <int BM>
+__device__ __forceinline__ void stage_cd_tiles(uint8_t* cs, float* wqs, const uint8_t* codes, const float* wq,
+                                               int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (r + i < rs) {
+                const int64_t off = (int64_t)(r + i) * n + c0 + k;
+                word |= (uint32_t)codes[off] << (8 * i);
+                wqs[k * LDW + r + i] = wq[off];
+            }
+        }
+        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+    }
+}
+
+template <int BM>
+__device__ __forceinline__ void unstage_cd_tiles(const uint8_t* cs, const float* wqs, uint8_t* codes, float* wq,
+                                                 int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        const uint32_t word = *reinterpret_cast<const uint32_t*>(cs + k * CSLD + r);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (r + i < rs) {
+                const int64_t off = (int64_t)(r + i) * n + c0 + k;
+                codes[off] = (uint8_t)(word >> (8 * i));
+                wq[off] = wqs[k * LDW + r + i];
+            }
+        }
+    }
+}
+
 // Shared-memory layout of the repair kernels: a body shared by the refit (group code tile + one 128-column
-// result tile) and the coordinate descent (sub-block code tile, gradient tile, W_hat tile and the sub-block
-// Hessian), per-row scalars, then the GEMM staging buffers.
+// result tile, which also holds the GEMM staging buffers) and the coordinate descent (sub-block code tile,
+// gradient tile - holding the staging buffers too when the sub-block is one GEMM tile wide -, W_hat tile and
+// the sub-block Hessian), then per-row scalars.
 constexpr int HSS_MAX_BYTES = 16384;  // sub-blocks up to 64 columns keep their whole Hessian block on chip
 
 struct RepairLayout {
-    size_t body, zrow, snew, accept, rowdelta, upd, stage, total;
+    size_t refit_tile, cd_gt, cd_stage, cd_wqs, cd_hss;  // body offsets
+    size_t body, zrow, snew, accept, rowdelta, upd, total;
 };
 
 static __host__ __device__ inline size_t cd_hss_bytes(int sbw) {
@@ -218,19 +281,31 @@ static __host__ __device__ inline size_t cd_hss_bytes(int sbw) {
 
 template <int BM>
 static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
-    constexpr int LD = RepairTiles<BM>::LD;
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    constexpr size_t STAGE = (size_t)RepairTiles<BM>::STAGE_FLOATS * 4;
+    static_assert((size_t)128 * LD * 4 >= STAGE, "the refit result tile holds the staging buffers");
     RepairLayout L;
     size_t gcap = (size_t)(g < 1024 ? g : 1024);
-    size_t refit = al16(gcap * BM) + al16((size_t)128 * LD * 4);
-    size_t cd = al16((size_t)sbw * BM) + 2 * al16((size_t)sbw * LD * 4) + cd_hss_bytes(sbw);
+    L.refit_tile = al16(gcap * CSLD);
+    size_t refit = L.refit_tile + al16((size_t)128 * LD * 4);
+    L.cd_gt = al16((size_t)sbw * CSLD);
+    size_t gt_bytes = al16((size_t)sbw * LD * 4);
+    if (sbw <= 128) {  // one GEMM tile: staging inside the gradient tile
+        L.cd_stage = L.cd_gt;
+        L.cd_wqs = L.cd_gt + (gt_bytes > STAGE ? gt_bytes : al16(STAGE));
+    } else {  // several GEMM tiles fill the gradient tile one after the other: separate staging
+        L.cd_stage = L.cd_gt + gt_bytes;
+        L.cd_wqs = L.cd_stage + al16(STAGE);
+    }
+    L.cd_hss = L.cd_wqs + al16((size_t)sbw * LDW * 4);
+    size_t cd = L.cd_hss + cd_hss_bytes(sbw);
     L.body = refit > cd ? refit : cd;
     L.zrow = L.body;
     L.snew = L.zrow + BM * 4;
     L.accept = L.snew + BM * 4;
     L.rowdelta = L.accept + BM * 4;
     L.upd = L.rowdelta + BM * 8;
-    L.stage = L.upd + BM * 8;
-    L.total = L.stage + (size_t)RepairTiles<BM>::STAGE_FLOATS * 4;
+    L.total = L.upd + BM * 8;
     return L;
 }
 
@@ -240,12 +315,16 @@ size_t repair_smem_bytes(int g, int sbw, int bm) {
 
 struct TileSmem {
     unsigned char* body;
+    float* refit_tile;  // [128][LD] (+ staging)
+    float* cd_gt;       // [sbw][LD]
+    float* cd_stage;
+    float* cd_wqs;      // [sbw][LDW]
+    float* cd_hss;
     float* zrow;
     float* snew;
     int* accept;
     double* rowdelta;
     unsigned long long* rowupd;
-    float* stage;
 };
 
 template <int BM>
@@ -253,12 +332,16 @@ __device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw
     const RepairLayout L = repair_layout<BM>(g, sbw);
     TileSmem t;
     t.body = raw;
+    t.refit_tile = reinterpret_cast<float*>(raw + L.refit_tile);
+    t.cd_gt = reinterpret_cast<float*>(raw + L.cd_gt);
+    t.cd_stage = reinterpret_cast<float*>(raw + L.cd_stage);
+    t.cd_wqs = reinterpret_cast<float*>(raw + L.cd_wqs);
+    t.cd_hss = reinterpret_cast<float*>(raw + L.cd_hss);
     t.zrow = reinterpret_cast<float*>(raw + L.zrow);
     t.snew = reinterpret_cast<float*>(raw + L.snew);
     t.accept = reinterpret_cast<int*>(raw + L.accept);
     t.rowdelta = reinterpret_cast<double*>(raw + L.rowdelta);
     t.rowupd = reinterpret_cast<unsigned long long*>(raw + L.upd);
-    t.stage = reinterpret_cast<float*>(raw + L.stage);
     return t;
 }
 
@@ -268,23 +351,19 @@ __device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw
 template <int BM>
 __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& sm, double& my_delta,
                            unsigned long long& my_upd) {
-    constexpr int LD = RepairTiles<BM>::LD;
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng;
-    const size_t gcap = (size_t)(g < 1024 ? g : 1024);
     float* E = ci.e + (int64_t)r0 * n;
     float* WQ = ci.wq + (int64_t)r0 * n;
     const uint8_t* CODES = ci.codes + (int64_t)r0 * n;
     float* SC = ci.scales + (int64_t)r0 * ng;
     const float* ZR = ci.zeros + (int64_t)r0 * ng;
     const float* H = ci.h;
-    uint8_t* cs = sm.body;                                              // [gcap][BM] codes of the group
-    float* tile = reinterpret_cast<float*>(sm.body + al16(gcap * BM));  // [128][LD] G, then u H_CC
+    uint8_t* cs = sm.body;        // [gcap][CSLD] codes of the group
+    float* tile = sm.refit_tile;  // [128][LD] G, then u H_CC; also the GEMM staging buffers
     for (int gi = 0; gi < ng; gi++) {
         const int c0 = gi * g, wd = min(g, n - c0);
-        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-            int rr = idx / wd, k = idx - rr * wd;
-            cs[k * BM + rr] = CODES[(int64_t)rr * n + c0 + k];
-        }
+        stage_codes<BM>(cs, CODES, n, c0, rs, wd);
         if (tid < BM) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
         __syncthreads();
         // num = sum_k u_k * G_k with G = E H[:, c0:c1]
@@ -292,11 +371,11 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             tile, sm.stage);
+                             tile, tile);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
-                    float u = __fsub_rn((float)cs[(t0 + k) * BM + tid], zr);
+                    float u = __fsub_rn((float)cs[(t0 + k) * CSLD + tid], zr);
                     num = __fadd_rn(num, __fmul_rn(u, tile[k * LD + tid]));
                 }
             }
@@ -306,11 +385,11 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
-                             wt, wd, tile, sm.stage);
+                             wt, wd, tile, tile);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
-                    float u = __fsub_rn((float)cs[(t0 + k) * BM + tid], zr);
+                    float u = __fsub_rn((float)cs[(t0 + k) * CSLD + tid], zr);
                     den = __fadd_rn(den, __fmul_rn(u, tile[k * LD + tid]));
                 }
             }
@@ -336,7 +415,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
             if (sm.accept[rr]) {
-                float u = __fsub_rn((float)cs[k * BM + rr], sm.zrow[rr]);
+                float u = __fsub_rn((float)cs[k * CSLD + rr], sm.zrow[rr]);
                 float ndq = __fmul_rn(sm.snew[rr], u);
                 int64_t off = (int64_t)rr * n + c0 + k;
                 E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
@@ -351,7 +430,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
 template <int BM>
 __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
                         unsigned long long& my_upd) {
-    constexpr int LD = RepairTiles<BM>::LD;
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
     float* E = ci.e + (int64_t)r0 * n;
     float* WQ = ci.wq + (int64_t)r0 * n;
@@ -360,20 +439,15 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
     const float* ZR = ci.zeros + (int64_t)r0 * ng;
     const float* H = ci.h;
     const int n_sel = ci.st->n_sel;
-    uint8_t* cs = sm.body;                                                 // [sbw][BM]
-    float* gt = reinterpret_cast<float*>(sm.body + al16((size_t)sbw * BM));  // [sbw][LD] block gradient
-    float* wqs = gt + (size_t)sbw * LD;                                    // [sbw][LD] W_hat
-    float* hss = wqs + (size_t)sbw * LD;                                   // [sbw][sbw] or its diagonal
+    uint8_t* cs = sm.body;     // [sbw][CSLD]
+    float* gt = sm.cd_gt;      // [sbw][LD] block gradient
+    float* wqs = sm.cd_wqs;    // [sbw][LDW] W_hat
+    float* hss = sm.cd_hss;    // [sbw][sbw] or its diagonal
     const bool hss_full = (size_t)sbw * sbw * 4 <= (size_t)HSS_MAX_BYTES;
     for (int si = 0; si < n_sel; si++) {
         const int s = ci.sel[si];
         const int c0 = s * sbw, wd = min(sbw, n - c0);
-        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-            int rr = idx / wd, k = idx - rr * wd;
-            int64_t off = (int64_t)rr * n + c0 + k;
-            cs[k * BM + rr] = CODES[off];
-            wqs[k * LD + rr] = WQ[off];
-        }
+        stage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         if (hss_full) {
             for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
                 int a = idx / wd, b = idx - a * wd;
@@ -385,7 +459,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             gt + (size_t)t0 * LD, sm.stage);
+                             gt + (size_t)t0 * LD, sm.cd_stage);
         }
         if (tid < rs) {
             const int r = tid;
@@ -403,7 +477,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                         z = ZR[(int64_t)r * ng + gi];
                     }
                     const float hjj = hss_full ? hss[jj * wd + jj] : hss[jj];
-                    const float cur = wqs[jj * LD + r];
+                    const float cur = wqs[jj * LDW + r];
                     const float gj = gt[jj * LD + r];
                     const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
                     float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
@@ -411,7 +485,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                     if (q > maxq) q = maxq;
                     const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
                     const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
-                    if (qc != cs[jj * BM + r]) {
+                    if (qc != cs[jj * CSLD + r]) {
                         // closed-form loss change, then the rank-1 gradient update (src/engine.rs:634-650)
                         const float de = __fsub_rn(cur, newdq);
                         const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
@@ -430,8 +504,8 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
                             }
                         }
-                        wqs[jj * LD + r] = newdq;
-                        cs[jj * BM + r] = qc;
+                        wqs[jj * LDW + r] = newdq;
+                        cs[jj * CSLD + r] = qc;
                         float* ep = &E[(int64_t)r * n + j];
                         *ep = __fadd_rn(*ep, de);
                         my_upd++;
@@ -442,12 +516,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
             }
         }
         __syncthreads();
-        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
-            int rr = idx / wd, k = idx - rr * wd;
-            int64_t off = (int64_t)rr * n + c0 + k;
-            CODES[off] = cs[k * BM + rr];
-            WQ[off] = wqs[k * LD + rr];
-        }
+        unstage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         __syncthreads();
     }
 }
