@@ -1,0 +1,705 @@
+// repair_core.cuh - the tile-level building blocks and the persistent kernels of phase 2 (the CDCL repair,
+// src/engine.rs:478-671), templated on the row-tile height BM (64 or 128).  Each BM is instantiated in its own
+// translation unit (repair_bm64.cu, repair_bm128.cu); repair.cu holds the statistics, mode A and dispatch.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "gemm_core.cuh"
+#include "kernels.h"
+
+namespace cdclq {
+
+static __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// ---------------------------------------------------------------------------------------------------------
+// GEMM tiles of the repair: result widths 128 (group refit), 64 and 32 (sub-blocks), K stages of 16.  The
+// staging buffers of a GEMM share shared memory with the tile that receives its result (the result is only
+// written after the last stage has been consumed), which keeps two 128-row CTAs on one SM.
+template <int BM>
+struct RepairTiles {
+    using W128 = Tile<BM, 128, 16>;
+    using W64 = Tile<BM, 64, 16>;
+    using W32 = Tile<BM, 32, 16>;
+    static constexpr int LD = BM + 4;    // [col][row] GEMM result tiles (16-byte aligned rows)
+    static constexpr int CSLD = BM + 4;  // [col][row] code tiles, bytes: consecutive columns start in distinct banks
+    static constexpr int LDW = BM + 1;   // [col][row] W_hat tile: consecutive columns start in distinct banks
+    static constexpr int STAGE_FLOATS = W128::STAGE_FLOATS > W64::STAGE_FLOATS
+                                            ? (W128::STAGE_FLOATS > W32::STAGE_FLOATS ? W128::STAGE_FLOATS
+                                                                                      : W32::STAGE_FLOATS)
+                                            : (W64::STAGE_FLOATS > W32::STAGE_FLOATS ? W64::STAGE_FLOATS
+                                                                                     : W32::STAGE_FLOATS);
+    static_assert(W128::ALD == LD && W64::ALD == LD && W32::ALD == LD, "result tiles share the A stride");
+};
+
+// A operand of the u H_CC product: A[k][row] = codes[k][row] - z[row] (src/engine.rs:553-558), staged from the
+// shared-memory code tile.  The code tile is k-major ([K][BM] bytes) like the A stage, so a thread converts
+// AP consecutive rows of one k and stores them with one vector store.
+template <class S>
+struct ACodes {
+    const uint8_t* cs;  // [K][BM + 4]
+    const float* zr;    // [BM], 16-byte aligned
+    int rows_valid;
+    int K;
+    static constexpr int TPR = S::BM / S::AP;  // threads per k row
+    static constexpr int LDC = S::BM + 4;
+    static_assert(S::AP % 4 == 0, "code rows are converted four at a time");
+    __device__ __forceinline__ void fetch(int k0, int tid, float (&r)[S::AP]) const {
+        const int kr = tid / TPR, c = (tid % TPR) * S::AP, k = k0 + kr;
+#pragma unroll
+        for (int v = 0; v < S::AP / 4; v++) {
+            uchar4 q = make_uchar4(0, 0, 0, 0);
+            if (k < K) q = *reinterpret_cast<const uchar4*>(cs + k * LDC + c + 4 * v);
+            const int b = c + 4 * v;
+            const float4 z = *reinterpret_cast<const float4*>(zr + b);
+            r[4 * v] = (k < K && b < rows_valid) ? __fsub_rn((float)q.x, z.x) : 0.0f;
+            r[4 * v + 1] = (k < K && b + 1 < rows_valid) ? __fsub_rn((float)q.y, z.y) : 0.0f;
+            r[4 * v + 2] = (k < K && b + 2 < rows_valid) ? __fsub_rn((float)q.z, z.z) : 0.0f;
+            r[4 * v + 3] = (k < K && b + 3 < rows_valid) ? __fsub_rn((float)q.w, z.w) : 0.0f;
+        }
+    }
+    __device__ __forceinline__ void store(float* As, int tid, const float (&r)[S::AP]) const {
+        const int kr = tid / TPR, c = (tid % TPR) * S::AP;
+#pragma unroll
+        for (int v = 0; v < S::AP / 4; v++)
+            *reinterpret_cast<float4*>(As + kr * S::ALD + c + 4 * v) =
+                make_float4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+    }
+};
+
+// The A operand of a repair GEMM: the error rows E (global) or the centred codes (shared memory).
+struct AFromE {
+    const float* e;
+    int64_t lde;
+    int rows_valid;
+    int K;
+    bool vec;
+    template <class S>
+    __device__ __forceinline__ AGlobal<S> make() const { return AGlobal<S>{e, lde, rows_valid, K, vec}; }
+};
+struct AFromCodes {
+    const uint8_t* cs;
+    const float* zr;
+    int rows_valid;
+    int K;
+    template <class S>
+    __device__ __forceinline__ ACodes<S> make() const { return ACodes<S>{cs, zr, rows_valid, K}; }
+};
+
+template <class S, class AM>
+__device__ __forceinline__ void gemm_to_tile_s(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd,
+                                               int K, float* out, float* stage) {
+    int ty, tx;
+    gemm_coords(threadIdx.x, ty, tx);
+    float acc[S::TM][S::TN];
+#pragma unroll
+    for (int i = 0; i < S::TM; i++)
+#pragma unroll
+        for (int j = 0; j < S::TN; j++) acc[i][j] = 0.0f;
+    const auto A = am.template make<S>();
+    BGlobal<S> Bop{b, ldb, col0, wd, K, (ldb % 4 == 0) && (col0 % 4 == 0)};
+    gemm_loader_a<S>(acc, A, Bop, K, stage);
+#pragma unroll
+    for (int j = 0; j < S::TN; j++) {
+        const int cc = TileMap<S>::col(tx, j);
+        if (cc < wd) {
+#pragma unroll
+            for (int v = 0; v < S::TM / 4; v++)
+                *reinterpret_cast<float4*>(out + cc * S::ALD + TileMap<S>::row(ty, 4 * v)) =
+                    make_float4(acc[4 * v][j], acc[4 * v + 1][j], acc[4 * v + 2][j], acc[4 * v + 3][j]);
+        }
+    }
+}
+
+// out[c][row] = (A B)[row][c] for c < wd (wd <= 128), B = b[k][col0 + c], via the narrowest fitting tile.
+// Ends synchronised.
+template <int BM, class AM>
+__device__ void gemm_to_tile(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
+                             float* stage) {
+    using RT = RepairTiles<BM>;
+    if (wd > 64)
+        gemm_to_tile_s<typename RT::W128>(am, b, ldb, col0, wd, K, out, stage);
+    else if (wd > 32)
+        gemm_to_tile_s<typename RT::W64>(am, b, ldb, col0, wd, K, out, stage);
+    else
+        gemm_to_tile_s<typename RT::W32>(am, b, ldb, col0, wd, K, out, stage);
+    __syncthreads();
+}
+
+// Tile staging between the row-major global matrices and the [col][row] shared-memory tiles.  A thread moves
+// one column of four consecutive rows: its global accesses are coalesced across the warp (consecutive
+// columns), and its shared-memory word lands in a distinct bank per column (strides CSLD / LDW).
+template <int BM>
+__device__ __forceinline__ void stage_codes(uint8_t* cs, const uint8_t* codes, int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if (r + i < rs) word |= (uint32_t)codes[(int64_t)(r + i) * n + c0 + k] << (8 * i);
+        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+    }
+}
+
+template <int BM>
+__device__ __forceinline__ void stage_cd_tiles(uint8_t* cs, float* wqs, const uint8_t* codes, const float* wq,
+                                               int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (r + i < rs) {
+                const int64_t off = (int64_t)(r + i) * n + c0 + k;
+                word |= (uint32_t)codes[off] << (8 * i);
+                wqs[k * LDW + r + i] = wq[off];
+            }
+        }
+        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+    }
+}
+
+template <int BM>
+__device__ __forceinline__ void unstage_cd_tiles(const uint8_t* cs, const float* wqs, uint8_t* codes, float* wq,
+                                                 int64_t n, int c0, int rs, int wd) {
+    constexpr int CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    const int quads = (rs + 3) >> 2;
+    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
+        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+        const uint32_t word = *reinterpret_cast<const uint32_t*>(cs + k * CSLD + r);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (r + i < rs) {
+                const int64_t off = (int64_t)(r + i) * n + c0 + k;
+                codes[off] = (uint8_t)(word >> (8 * i));
+                wq[off] = wqs[k * LDW + r + i];
+            }
+        }
+    }
+}
+
+// Shared-memory layout of the repair kernels: a body shared by the refit (group code tile + one 128-column
+// result tile, which also holds the GEMM staging buffers) and the coordinate descent (sub-block code tile,
+// gradient tile - holding the staging buffers too when the sub-block is one GEMM tile wide -, W_hat tile and
+// the sub-block Hessian), then per-row scalars.
+constexpr int HSS_MAX_BYTES = 16384;  // sub-blocks up to 64 columns keep their whole Hessian block on chip
+
+struct RepairLayout {
+    size_t refit_tile, cd_gt, cd_stage, cd_wqs, cd_hss;  // body offsets
+    size_t body, zrow, snew, accept, rowdelta, upd, total;
+};
+
+static __host__ __device__ inline size_t cd_hss_bytes(int sbw) {
+    size_t full = (size_t)sbw * sbw * 4;
+    return full <= (size_t)HSS_MAX_BYTES ? al16(full) : al16((size_t)sbw * 4);
+}
+
+template <int BM>
+static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    constexpr size_t STAGE = (size_t)RepairTiles<BM>::STAGE_FLOATS * 4;
+    static_assert((size_t)128 * LD * 4 >= STAGE, "the refit result tile holds the staging buffers");
+    RepairLayout L;
+    size_t gcap = (size_t)(g < 1024 ? g : 1024);
+    L.refit_tile = al16(gcap * CSLD);
+    size_t refit = L.refit_tile + al16((size_t)128 * LD * 4);
+    L.cd_gt = al16((size_t)sbw * CSLD);
+    size_t gt_bytes = al16((size_t)sbw * LD * 4);
+    if (sbw <= 128) {  // one GEMM tile: staging inside the gradient tile
+        L.cd_stage = L.cd_gt;
+        L.cd_wqs = L.cd_gt + (gt_bytes > STAGE ? gt_bytes : al16(STAGE));
+    } else {  // several GEMM tiles fill the gradient tile one after the other: separate staging
+        L.cd_stage = L.cd_gt + gt_bytes;
+        L.cd_wqs = L.cd_stage + al16(STAGE);
+    }
+    L.cd_hss = L.cd_wqs + al16((size_t)sbw * LDW * 4);
+    size_t cd = L.cd_hss + cd_hss_bytes(sbw);
+    L.body = refit > cd ? refit : cd;
+    L.zrow = L.body;
+    L.snew = L.zrow + BM * 4;
+    L.accept = L.snew + BM * 4;
+    L.rowdelta = L.accept + BM * 4;
+    L.upd = L.rowdelta + BM * 8;
+    L.total = L.upd + BM * 8;
+    return L;
+}
+
+
+struct TileSmem {
+    unsigned char* body;
+    float* refit_tile;  // [128][LD] (+ staging)
+    float* cd_gt;       // [sbw][LD]
+    float* cd_stage;
+    float* cd_wqs;      // [sbw][LDW]
+    float* cd_hss;
+    float* zrow;
+    float* snew;
+    int* accept;
+    double* rowdelta;
+    unsigned long long* rowupd;
+};
+
+template <int BM>
+__device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw) {
+    const RepairLayout L = repair_layout<BM>(g, sbw);
+    TileSmem t;
+    t.body = raw;
+    t.refit_tile = reinterpret_cast<float*>(raw + L.refit_tile);
+    t.cd_gt = reinterpret_cast<float*>(raw + L.cd_gt);
+    t.cd_stage = reinterpret_cast<float*>(raw + L.cd_stage);
+    t.cd_wqs = reinterpret_cast<float*>(raw + L.cd_wqs);
+    t.cd_hss = reinterpret_cast<float*>(raw + L.cd_hss);
+    t.zrow = reinterpret_cast<float*>(raw + L.zrow);
+    t.snew = reinterpret_cast<float*>(raw + L.snew);
+    t.accept = reinterpret_cast<int*>(raw + L.accept);
+    t.rowdelta = reinterpret_cast<double*>(raw + L.rowdelta);
+    t.rowupd = reinterpret_cast<unsigned long long*>(raw + L.upd);
+    return t;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Closed-form scale refit of every (row, group) of the rows [r0, r0 + rs) of a chunk, groups in order
+// (src/engine.rs:534-589).  Thread r < rs accumulates its row's accepted loss deltas and refits.
+template <int BM>
+__device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& sm, double& my_delta,
+                           unsigned long long& my_upd) {
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD;
+    const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng;
+    float* E = ci.e + (int64_t)r0 * n;
+    float* WQ = ci.wq + (int64_t)r0 * n;
+    const uint8_t* CODES = ci.codes + (int64_t)r0 * n;
+    float* SC = ci.scales + (int64_t)r0 * ng;
+    const float* ZR = ci.zeros + (int64_t)r0 * ng;
+    const float* H = ci.h;
+    uint8_t* cs = sm.body;        // [gcap][CSLD] codes of the group
+    float* tile = sm.refit_tile;  // [128][LD] G, then u H_CC; also the GEMM staging buffers
+    for (int gi = 0; gi < ng; gi++) {
+        const int c0 = gi * g, wd = min(g, n - c0);
+        stage_codes<BM>(cs, CODES, n, c0, rs, wd);
+        if (tid < BM) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
+        __syncthreads();
+        // num = sum_k u_k * G_k with G = E H[:, c0:c1]
+        float num = 0.0f, den = 0.0f;
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                             tile, tile);
+            if (tid < rs) {
+                const float zr = sm.zrow[tid];
+                for (int k = 0; k < wt; k++) {
+                    float u = __fsub_rn((float)cs[(t0 + k) * CSLD + tid], zr);
+                    num = __fadd_rn(num, __fmul_rn(u, tile[k * LD + tid]));
+                }
+            }
+            __syncthreads();
+        }
+        // den = sum_k u_k * (u H_CC)_k
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            gemm_to_tile<BM>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
+                             wt, wd, tile, tile);
+            if (tid < rs) {
+                const float zr = sm.zrow[tid];
+                for (int k = 0; k < wt; k++) {
+                    float u = __fsub_rn((float)cs[(t0 + k) * CSLD + tid], zr);
+                    den = __fadd_rn(den, __fmul_rn(u, tile[k * LD + tid]));
+                }
+            }
+            __syncthreads();
+        }
+        if (tid < BM) sm.accept[tid] = 0;
+        if (tid < rs && den > 1e-30f) {
+            const float s_old = SC[(int64_t)tid * ng + gi];
+            float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
+            if (!(s_new >= kF16MinNormal)) s_new = kF16MinNormal;  // f32::max(x, MIN)
+            const float d = __fsub_rn(s_new, s_old);
+            const float dlf = __fadd_rn(__fmul_rn(__fmul_rn(-2.0f, d), num), __fmul_rn(__fmul_rn(d, d), den));
+            const double dl = (double)dlf;
+            if (dl < 0.0) {
+                SC[(int64_t)tid * ng + gi] = s_new;
+                sm.snew[tid] = s_new;
+                sm.accept[tid] = 1;
+                my_delta = __dadd_rn(my_delta, dl);
+                my_upd++;
+            }
+        }
+        __syncthreads();
+        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+            int rr = idx / wd, k = idx - rr * wd;
+            if (sm.accept[rr]) {
+                float u = __fsub_rn((float)cs[k * CSLD + rr], sm.zrow[rr]);
+                float ndq = __fmul_rn(sm.snew[rr], u);
+                int64_t off = (int64_t)rr * n + c0 + k;
+                E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
+                WQ[off] = ndq;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Coordinate descent over the selected sub-blocks for rows [r0, r0 + rs) (src/engine.rs:600-658).
+template <int BM>
+__device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
+                        unsigned long long& my_upd) {
+    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
+    float* E = ci.e + (int64_t)r0 * n;
+    float* WQ = ci.wq + (int64_t)r0 * n;
+    uint8_t* CODES = ci.codes + (int64_t)r0 * n;
+    const float* SC = ci.scales + (int64_t)r0 * ng;
+    const float* ZR = ci.zeros + (int64_t)r0 * ng;
+    const float* H = ci.h;
+    const int n_sel = ci.st->n_sel;
+    uint8_t* cs = sm.body;     // [sbw][CSLD]
+    float* gt = sm.cd_gt;      // [sbw][LD] block gradient
+    float* wqs = sm.cd_wqs;    // [sbw][LDW] W_hat
+    float* hss = sm.cd_hss;    // [sbw][sbw] or its diagonal
+    const bool hss_full = (size_t)sbw * sbw * 4 <= (size_t)HSS_MAX_BYTES;
+    for (int si = 0; si < n_sel; si++) {
+        const int s = ci.sel[si];
+        const int c0 = s * sbw, wd = min(sbw, n - c0);
+        stage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
+        if (hss_full) {
+            for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
+                int a = idx / wd, b = idx - a * wd;
+                hss[idx] = __ldg(H + (int64_t)(c0 + a) * n + c0 + b);
+            }
+        } else {
+            for (int a = tid; a < wd; a += blockDim.x) hss[a] = __ldg(H + (int64_t)(c0 + a) * n + c0 + a);
+        }
+        for (int t0 = 0; t0 < wd; t0 += 128) {
+            int wt = min(128, wd - t0);
+            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                             gt + (size_t)t0 * LD, sm.cd_stage);
+        }
+        if (tid < rs) {
+            const int r = tid;
+            for (int sw = 0; sw < cd_sweeps; sw++) {
+                bool changed = false;
+                int cur_gi = -1;
+                float sc = 1.0f, z = 0.0f, maxq = 1.0f;
+                for (int jj = 0; jj < wd; jj++) {
+                    const int j = c0 + jj;
+                    const int gi = j / g;
+                    if (gi != cur_gi) {
+                        cur_gi = gi;
+                        maxq = (float)((1u << ci.gbits[gi]) - 1u);
+                        sc = SC[(int64_t)r * ng + gi];
+                        z = ZR[(int64_t)r * ng + gi];
+                    }
+                    const float hjj = hss_full ? hss[jj * wd + jj] : hss[jj];
+                    const float cur = wqs[jj * LDW + r];
+                    const float gj = gt[jj * LD + r];
+                    const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
+                    float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
+                    if (q < 0.0f) q = 0.0f;
+                    if (q > maxq) q = maxq;
+                    const float newdq = __fmul_rn(sc, __fsub_rn(q, z));
+                    const uint8_t qc = (q == q) ? (uint8_t)q : (uint8_t)0;
+                    if (qc != cs[jj * CSLD + r]) {
+                        // closed-form loss change, then the rank-1 gradient update (src/engine.rs:634-650)
+                        const float de = __fsub_rn(cur, newdq);
+                        const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
+                        const float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
+                        my_delta = __dadd_rn(my_delta, (double)__fadd_rn(t1, t2));
+                        if (hss_full) {
+                            const float* hrow = hss + jj * wd;
+                            for (int kk = 0; kk < wd; kk++) {
+                                float* gp = &gt[kk * LD + r];
+                                *gp = __fadd_rn(*gp, __fmul_rn(de, hrow[kk]));
+                            }
+                        } else {
+                            const float* hrow = H + (int64_t)j * n + c0;
+                            for (int kk = 0; kk < wd; kk++) {
+                                float* gp = &gt[kk * LD + r];
+                                *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
+                            }
+                        }
+                        wqs[jj * LDW + r] = newdq;
+                        cs[jj * CSLD + r] = qc;
+                        float* ep = &E[(int64_t)r * n + j];
+                        *ep = __fadd_rn(*ep, de);
+                        my_upd++;
+                        changed = true;
+                    }
+                }
+                if (!changed) break;
+            }
+        }
+        __syncthreads();
+        unstage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
+        __syncthreads();
+    }
+}
+
+// Sum of the tile's per-row results, rows in order; valid in thread 0.  Ends synchronised.
+template <int BM>
+__device__ __forceinline__ void tile_reduce(int rs, const TileSmem& sm, double my_delta, unsigned long long my_upd,
+                                            double& d, unsigned long long& u) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    if (tid < BM) {
+        sm.rowdelta[tid] = (tid < rs) ? my_delta : 0.0;
+        sm.rowupd[tid] = (tid < rs) ? my_upd : 0ull;
+    }
+    __syncthreads();
+    d = 0.0;
+    u = 0ull;
+    if (tid == 0) {
+        for (int r = 0; r < rs; r++) {
+            d = __dadd_rn(d, sm.rowdelta[r]);
+            u += sm.rowupd[r];
+        }
+    }
+    __syncthreads();
+}
+
+// One tile of one pass (refit then coordinate descent, or the final refit alone); the tile's delta and
+// update count are valid in thread 0.
+template <int BM>
+__device__ __forceinline__ void run_tile(const ChunkInfo& ci, int r0, int rs, const RepairParams& rp, bool final_refit,
+                                         const TileSmem& sm, double& d, unsigned long long& u) {
+    double my_delta = 0.0;
+    unsigned long long my_upd = 0ull;
+    if (rp.do_refit) refit_tile<BM>(ci, r0, rs, sm, my_delta, my_upd);
+    if (rp.do_cd && !final_refit) cd_tile<BM>(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+    tile_reduce<BM>(rs, sm, my_delta, my_upd, d, u);
+}
+
+// The reference's stop rule after a pass (src/engine.rs:660-665), in thread 0 / one thread.
+__device__ __forceinline__ void apply_pass(ChunkState* st, double pass_delta, unsigned long long pass_upd, double tol) {
+    st->loss_delta = __dadd_rn(st->loss_delta, pass_delta);
+    st->updates += pass_upd;
+    st->passes += 1;
+    const double gain = __dsub_rn(st->prev_delta, st->loss_delta);
+    st->prev_delta = st->loss_delta;
+    if (pass_upd == 0ull || gain < tol * __dadd_rn(st->loss_gptq, st->loss_delta)) st->done = 1;
+}
+
+
+template <int BM>
+__global__ void __launch_bounds__(256, 2) repair_persistent_kernel(const ChunkInfo* __restrict__ chunks, int nchunks,
+                                                                   RepairParams rp, int* __restrict__ counter) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int s_chunk, s_done;
+    __shared__ ChunkInfo ci;  // chunk descriptor kept on chip (not in registers across the tile loops)
+    const int tid = threadIdx.x;
+    for (;;) {
+        if (tid == 0) {
+            s_chunk = atomicAdd(counter, 1);
+            if (s_chunk < nchunks) ci = chunks[s_chunk];
+        }
+        __syncthreads();
+        const int c = s_chunk;
+        if (c >= nchunks) return;
+        ChunkState* st = ci.st;
+        const TileSmem sm = tile_smem<BM>(smem_raw, ci.g, ci.sbw);
+        if (tid == 0) s_done = st->done;
+        __syncthreads();
+        for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
+            double pd = 0.0;
+            unsigned long long pu = 0ull;
+            for (int r0 = 0; r0 < ci.rows; r0 += BM) {
+                double d;
+                unsigned long long u;
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, false, sm, d, u);
+                if (tid == 0) {
+                    pd = __dadd_rn(pd, d);
+                    pu += u;
+                }
+            }
+            if (tid == 0) {
+                apply_pass(st, pd, pu, rp.tol);
+                s_done = st->done;
+            }
+            __syncthreads();
+        }
+        if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
+            double fd = 0.0;
+            unsigned long long fu = 0ull;
+            for (int r0 = 0; r0 < ci.rows; r0 += BM) {
+                double d;
+                unsigned long long u;
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, true, sm, d, u);
+                if (tid == 0) {
+                    fd = __dadd_rn(fd, d);
+                    fu += u;
+                }
+            }
+            if (tid == 0) {
+                st->loss_delta = __dadd_rn(st->loss_delta, fd);
+                st->updates += fu;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Mode C - persistent clusters: a cluster of 2 CTAs takes a whole row chunk of several tiles (heaviest first);
+// CTA rank r handles the chunk's tiles r, r+2, ...  A row chunk's passes are the latency-critical unit, and
+// splitting its rows over two SMs halves that critical path.  At the end of each pass the tiles' partial sums
+// are written into rank 0's shared memory (distributed shared memory), rank 0 adds them in tile order - the
+// order of mode B - applies the stop rule and writes the decision back into rank 1; hardware cluster barriers
+// order these steps.
+
+constexpr int RP_MAX_TILES = RP_MAX_TILES_PER_CHUNK;
+
+template <int BM>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
+    repair_cluster_kernel(const ChunkInfo* __restrict__ chunks, int nchunks, RepairParams rp, int* __restrict__ counter) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int s_chunk, s_done;
+    __shared__ ChunkInfo ci;
+    __shared__ double s_tile_delta[RP_MAX_TILES];
+    __shared__ unsigned long long s_tile_upd[RP_MAX_TILES];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int tid = threadIdx.x;
+    int* chunk0 = cluster.map_shared_rank(&s_chunk, 0);
+    int* done1 = cluster.map_shared_rank(&s_done, 1);
+    double* tdelta0 = cluster.map_shared_rank(&s_tile_delta[0], 0);
+    unsigned long long* tupd0 = cluster.map_shared_rank(&s_tile_upd[0], 0);
+    for (;;) {
+        if (rank == 0 && tid == 0) s_chunk = atomicAdd(counter, 1);
+        cluster.sync();
+        const int c = *chunk0;
+        if (tid == 0 && c < nchunks) ci = chunks[c];
+        cluster.sync();  // every rank has read rank 0's s_chunk before anyone may leave or overwrite it
+        if (c >= nchunks) return;
+        ChunkState* st = ci.st;
+        const TileSmem sm = tile_smem<BM>(smem_raw, ci.g, ci.sbw);
+        const int ntiles = (ci.rows + BM - 1) / BM;
+        if (tid == 0) s_done = st->done;
+        __syncthreads();
+        for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
+            for (int t = rank; t < ntiles; t += 2) {
+                const int r0 = t * BM;
+                double d;
+                unsigned long long u;
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, false, sm, d, u);
+                if (tid == 0) {
+                    tdelta0[t] = d;
+                    tupd0[t] = u;
+                }
+            }
+            cluster.sync();  // all tile partials are in rank 0
+            if (rank == 0 && tid == 0) {
+                double pd = 0.0;
+                unsigned long long pu = 0ull;
+                for (int t = 0; t < ntiles; t++) {
+                    pd = __dadd_rn(pd, s_tile_delta[t]);
+                    pu += s_tile_upd[t];
+                }
+                apply_pass(st, pd, pu, rp.tol);
+                s_done = st->done;
+                *done1 = st->done;
+            }
+            cluster.sync();  // the decision is visible in both ranks
+        }
+        if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
+            for (int t = rank; t < ntiles; t += 2) {
+                const int r0 = t * BM;
+                double d;
+                unsigned long long u;
+                run_tile<BM>(ci, r0, min(BM, ci.rows - r0), rp, true, sm, d, u);
+                if (tid == 0) {
+                    tdelta0[t] = d;
+                    tupd0[t] = u;
+                }
+            }
+            cluster.sync();
+            if (rank == 0 && tid == 0) {
+                double fd = 0.0;
+                unsigned long long fu = 0ull;
+                for (int t = 0; t < ntiles; t++) {
+                    fd = __dadd_rn(fd, s_tile_delta[t]);
+                    fu += s_tile_upd[t];
+                }
+                st->loss_delta = __dadd_rn(st->loss_delta, fd);
+                st->updates += fu;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+
+static inline int set_repair_smem(const void* fn, size_t smem) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair smem attribute");
+}
+
+static inline int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+template <int BM>
+static int launch_cluster_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                             int* counter_dev, cudaStream_t st) {
+    int rc = set_repair_smem((const void*)repair_cluster_kernel<BM>, smem);
+    if (rc) return rc;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_cluster_kernel<BM>, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    int clusters = sm_count() * per_sm / 2;
+    if (clusters > nchunks) clusters = nchunks;
+    if (clusters < 1) clusters = 1;
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
+    CDCLQ_LAUNCH(repair_cluster_kernel<BM>, 2 * clusters, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_cluster_kernel launch");
+}
+
+template <int BM>
+static int launch_persistent_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                                int* counter_dev, cudaStream_t st) {
+    int rc = set_repair_smem((const void*)repair_persistent_kernel<BM>, smem);
+    if (rc) return rc;
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel<BM>, 256, smem);
+    if (per_sm < 1) per_sm = 1;
+    int grid = sm_count() * per_sm;
+    if (grid > nchunks) grid = nchunks;
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
+    CDCLQ_LAUNCH(repair_persistent_kernel<BM>, grid, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_persistent_kernel launch");
+}
+
+// CTAs of the persistent kernel that fit on one SM with `smem` bytes of dynamic shared memory (0 on error).
+template <int BM>
+static int persistent_ctas_per_sm(size_t smem) {
+    if (set_repair_smem((const void*)repair_persistent_kernel<BM>, smem)) {
+        cudaGetLastError();
+        return 0;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel<BM>, 256, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return per_sm;
+}
+
+// Per-BM entry points (repair_bm64.cu, repair_bm128.cu).
+int launch_repair_persistent_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                                  int* counter_dev, cudaStream_t st);
+int launch_repair_cluster_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                               int* counter_dev, cudaStream_t st);
+int launch_repair_persistent_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                                   int* counter_dev, cudaStream_t st);
+int launch_repair_cluster_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                                int* counter_dev, cudaStream_t st);
+int repair_persistent_ctas_per_sm_bm128(size_t smem);
+
+}  // namespace cdclq
