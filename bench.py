@@ -21,9 +21,11 @@ Legs:
             N = 1 only
   --impl reference  the oracle port on the host cores (the Rust reference cannot be built here), same sample
 
-N > 1: one process per GPU (torchrun); every layer's rows are split across ranks in whole row chunks (rows are
-independent and row chunks are the reference's unit of conflict selection and stopping), so the result is
-identical to N = 1; the per-layer losses are all-reduced over NCCL.  Weak/strong: strong (the model is fixed).
+N > 1: one process per GPU (torchrun), cdclq.pipeline.ModelBatch: every layer's rows are split across ranks in
+whole row chunks (rows are independent and row chunks are the reference's unit of conflict selection and
+stopping); the 88 factorisations are spread over the ranks (longest-processing-time on n^3) and each factor U
+is broadcast from its owner over NCCL; the result is identical to N = 1; the per-layer losses are all-reduced
+over NCCL.  Weak/strong: strong (the model is fixed).
 """
 import argparse
 import ctypes
@@ -116,74 +118,6 @@ def generate(torch, device, n_layers=N_LAYERS, tokens=TOKENS):
     H = [make_hessian(n, 1000 + i, tokens, torch, device) for i, (_, n) in enumerate(inputs)]
     W = [make_weight(d_out, d_in, 50000 + i, torch, device) for i, (_, d_out, d_in, _) in enumerate(layers)]
     return layers, inputs, H, W
-
-
-# ------------------------------------------------------------------------------------------------------------
-def shard_rows(d_out, rank, world):
-    """Contiguous row range of this rank, in whole row chunks."""
-    chunks = (d_out + ROW_CHUNK - 1) // ROW_CHUNK
-    c0 = chunks * rank // world
-    c1 = chunks * (rank + 1) // world
-    return min(c0 * ROW_CHUNK, d_out), min(c1 * ROW_CHUNK, d_out)
-
-
-class Batch:
-    """Preallocated outputs + C descriptor tables for one cdclq_quantize_batch call."""
-
-    def __init__(self, torch, layers, inputs, H, W, cfg, rank, world, on_device):
-        from cdclq.abi import CBatchInput, CBatchLayer, CLayerStats, num_groups
-
-        self.cfg = cfg
-        self.on_device = on_device
-        self.keep = []
-        self.ins = (CBatchInput * len(inputs))()
-        for i, (_, n) in enumerate(inputs):
-            h = H[i]
-            self.keep.append(h)
-            self.ins[i].h = h.data_ptr()
-            self.ins[i].n = n
-        rows = []
-        for (name, d_out, d_in, inp), w in zip(layers, W):
-            r0, r1 = shard_rows(d_out, rank, world)
-            if r1 > r0:
-                rows.append((name, d_out, d_in, inp, w, r0, r1))
-        self.lys = (CBatchLayer * len(rows))()
-        self.stats = [CLayerStats() for _ in rows]
-        self.outs = []
-        self.h2d_bytes = sum(int(h.numel()) * 4 for h in H)
-        self.d2h_bytes = 0
-        dev = "cuda" if on_device else "cpu"
-        for i, (name, d_out, d_in, inp, w, r0, r1) in enumerate(rows):
-            ng = num_groups(cfg, d_in)
-            rs = r1 - r0
-            wv = w[r0:r1]
-            self.keep.append(wv)
-            o = dict(perm=np.zeros(d_in, np.uint32), gbits=np.zeros(ng, np.uint8),
-                     codes=torch.empty(rs, d_in, dtype=torch.uint8, device=dev, pin_memory=not on_device),
-                     scales=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device),
-                     zeros=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device))
-            self.outs.append(o)
-            L = self.lys[i]
-            L.w = wv.data_ptr()
-            L.d_out = rs
-            L.input = inp
-            L.perm = o["perm"].ctypes.data
-            L.gbits = o["gbits"].ctypes.data
-            L.codes = o["codes"].data_ptr()
-            L.scales = o["scales"].data_ptr()
-            L.zeros = o["zeros"].data_ptr()
-            L.stats = ctypes.pointer(self.stats[i])
-            self.h2d_bytes += rs * d_in * 4
-            self.d2h_bytes += rs * d_in + 2 * rs * ng * 4 + d_in * 4 + ng
-        self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1) in rows)
-
-    def run(self, stream_handle):
-        import cdclq
-
-        c = self.cfg.to_c()
-        cdclq._lib.check(cdclq.lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys),
-                                                          ctypes.byref(c), 1 if self.on_device else 0,
-                                                          ctypes.c_void_p(stream_handle)))
 
 
 # ------------------------------------------------------------------------------------------------------------
@@ -381,7 +315,7 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
 
@@ -392,13 +326,14 @@ def main():
         return
 
     import cdclq
+    from cdclq.pipeline import ModelBatch
 
     cdclq.lib()
     cfg = bench_config()
     device = "cuda"
     layers, inputs, H, W = generate(torch, device, args.layers)
     total_weights = sum(l[1] * l[2] for l in layers)
-    batch = Batch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True)
+    batch = ModelBatch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -442,7 +377,7 @@ def main():
     # ---- e2e through the public C ABI with pinned host buffers
     Hh = [h.cpu().pin_memory() for h in H]
     Wh = [w.cpu().pin_memory() for w in W]
-    hb = Batch(torch, layers, inputs, Hh, Wh, cfg, rank, world, on_device=False)
+    hb = ModelBatch(torch, layers, inputs, Hh, Wh, cfg, rank, world, on_device=False)
     hb.run(0)  # warm the host path once
     torch.cuda.synchronize()
     barrier()

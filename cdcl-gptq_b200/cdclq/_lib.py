@@ -33,6 +33,9 @@ SIGNATURES = {
                                       ctypes.POINTER(CLayerStats), P]),
     "cdclq_row_chunk": (SZ, [CFG, SZ]),
     "cdclq_quantize_batch": (I32, [ctypes.POINTER(CBatchInput), SZ, ctypes.POINTER(CBatchLayer), SZ, CFG, I32, P]),
+    "cdclq_prepare_factors": (I32, [ctypes.POINTER(CBatchInput), SZ, P, SZ, CFG, P, I32, P]),
+    "cdclq_quantize_batch_prepared": (I32, [ctypes.POINTER(CBatchInput), SZ, P, ctypes.POINTER(CBatchLayer), SZ, CFG,
+                                            I32, P]),
     "cdclq_cholesky_lower": (I32, [P, SZ]),
     "cdclq_tri_inverse_lower": (I32, [P, SZ, P]),
     "cdclq_upper_chol_of_inverse": (I32, [P, SZ, P]),

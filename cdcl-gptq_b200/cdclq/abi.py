@@ -94,6 +94,8 @@ class CRunProfile(ctypes.Structure):
         ("factorisations", ctypes.c_uint64),
         ("weights", ctypes.c_uint64),
         ("launches", ctypes.c_uint64),
+        ("factor_batches", ctypes.c_uint64),
+        ("ms_host", ctypes.c_double),
     ]
 
     def as_dict(self):

@@ -1,0 +1,142 @@
+"""`pipeline.rs` counterpart: a model's layers quantized as one batch, optionally over several GPUs.
+
+The reference quantizes layer after layer on one host, its jobs sorted by Hessian owner so that consecutive
+layers reuse one factorisation (src/pipeline.rs:92-175).  Here all layers of a model go through one
+cdclq_quantize_batch call (every distinct input factorised once), and with several GPUs - one process per
+GPU, torch.distributed over NCCL as the plumbing - the work is split along the independence structure of the
+algorithm:
+
+  * rows: every layer's rows are split in whole row chunks, a contiguous range per rank (rows are
+    independent, src/engine.rs:9-15; conflict selection and the tol stop are per row chunk,
+    src/engine.rs:480-511, 660-665, so chunk boundaries must not move);
+  * factorisations: the distinct inputs are assigned to ranks by longest-processing-time on n^3 (Cholesky +
+    triangular inverse), each rank factorises its share (cdclq_prepare_factors) and every factor U is then
+    broadcast from its owner, so no rank repeats another's factorisation;
+  * statistics: the per-layer sums of the row shards are additive (the caller all-reduces them).
+
+Results are bit-identical to a single-GPU run: the factorisation is deterministic, and a row's computation
+does not depend on which rank holds it.
+"""
+import ctypes
+
+import numpy as np
+
+from ._lib import check, lib
+from .abi import CBatchInput, CBatchLayer, CLayerStats, num_groups
+
+
+def shard_rows(d_out, row_chunk, rank, world):
+    """Contiguous row range [r0, r1) of `rank`, in whole row chunks of `row_chunk` rows."""
+    chunks = (d_out + row_chunk - 1) // row_chunk
+    c0 = chunks * rank // world
+    c1 = chunks * (rank + 1) // world
+    return min(c0 * row_chunk, d_out), min(c1 * row_chunk, d_out)
+
+
+def assign_factorisations(ns, world):
+    """Owner rank of each distinct input: longest-processing-time scheduling on the n^3 cost of its
+    factorisation (largest first, ties by index), each to the least-loaded rank (ties to the lowest rank)."""
+    owner = [0] * len(ns)
+    load = [0.0] * world
+    for i in sorted(range(len(ns)), key=lambda i: (-ns[i], i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        owner[i] = r
+        load[r] += float(ns[i]) ** 3
+    return owner
+
+
+def exchange_factors(factors, owner):
+    """Broadcast every factor from its owner rank, inputs in index order (every rank takes the same collective
+    steps in the same order).  `factors` are tensors on the process group's device."""
+    import torch.distributed as dist
+
+    for i, u in enumerate(factors):
+        dist.broadcast(u, src=owner[i])
+
+
+class ModelBatch:
+    """Descriptor tables and caller-allocated outputs for one model on one rank.
+
+    layers: [(name, d_out, d_in, input index)]; inputs: [(name, n)]; H: per input an n x n f32 tensor; W: per
+    layer a d_out x d_in f32 tensor (original column order).  All tensors on the device (on_device=True) or
+    all in (pinned) host memory (on_device=False, copies inside the library).  With world > 1 the rank keeps
+    the rows shard_rows() gives it, and `run` needs torch.distributed initialised (NCCL).
+    """
+
+    def __init__(self, torch, layers, inputs, H, W, cfg, rank=0, world=1, on_device=True, distribute_factors=True):
+        self.torch = torch
+        self.cfg = cfg
+        self.rank, self.world = rank, world
+        self.on_device = on_device
+        self.keep = []
+        self.ins = (CBatchInput * len(inputs))()
+        for i, (_, n) in enumerate(inputs):
+            self.keep.append(H[i])
+            self.ins[i].h = H[i].data_ptr()
+            self.ins[i].n = n
+        rc = cfg.row_chunk
+        if rc <= 0 and world > 1:
+            raise ValueError("multi-GPU row sharding needs a pinned row_chunk (row chunks must not move)")
+        rows = []
+        for (name, d_out, d_in, inp), w in zip(layers, W):
+            r0, r1 = shard_rows(d_out, rc, rank, world) if world > 1 else (0, d_out)
+            if r1 > r0:
+                rows.append((name, d_out, d_in, inp, w, r0, r1))
+        self.names = [r[0] for r in rows]
+        self.shards = [(r[5], r[6]) for r in rows]
+        self.lys = (CBatchLayer * len(rows))()
+        self.stats = [CLayerStats() for _ in rows]
+        self.outs = []
+        self.h2d_bytes = sum(int(h.numel()) * 4 for h in H)
+        self.d2h_bytes = 0
+        dev = "cuda" if on_device else "cpu"
+        for i, (name, d_out, d_in, inp, w, r0, r1) in enumerate(rows):
+            ng = num_groups(cfg, d_in)
+            rs = r1 - r0
+            wv = w[r0:r1]
+            self.keep.append(wv)
+            o = dict(perm=np.zeros(d_in, np.uint32), gbits=np.zeros(ng, np.uint8),
+                     codes=torch.empty(rs, d_in, dtype=torch.uint8, device=dev, pin_memory=not on_device),
+                     scales=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device),
+                     zeros=torch.empty(rs, ng, dtype=torch.float32, device=dev, pin_memory=not on_device))
+            self.outs.append(o)
+            L = self.lys[i]
+            L.w = wv.data_ptr()
+            L.d_out = rs
+            L.input = inp
+            L.perm = o["perm"].ctypes.data
+            L.gbits = o["gbits"].ctypes.data
+            L.codes = o["codes"].data_ptr()
+            L.scales = o["scales"].data_ptr()
+            L.zeros = o["zeros"].data_ptr()
+            L.stats = ctypes.pointer(self.stats[i])
+            self.h2d_bytes += rs * d_in * 4
+            self.d2h_bytes += rs * d_in + 2 * rs * ng * 4 + d_in * 4 + ng
+        self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1) in rows)
+
+        # factorisations spread over the ranks: factor buffers for every input, owners by LPT on n^3
+        self.distributed = world > 1 and distribute_factors and cfg.skeleton_pct <= 0.0
+        if self.distributed:
+            ns = [n for (_, n) in inputs]
+            self.owner = assign_factorisations(ns, world)
+            self.u = [torch.empty(n, n, dtype=torch.float32, device="cuda") for n in ns]
+            self.mine = [i for i in range(len(ns)) if self.owner[i] == rank]
+            self._which = (ctypes.c_size_t * max(1, len(self.mine)))(*self.mine)
+            self._u_out = (ctypes.c_void_p * max(1, len(self.mine)))(*[self.u[i].data_ptr() for i in self.mine])
+            self._u_in = (ctypes.c_void_p * len(ns))(*[u.data_ptr() for u in self.u])
+            self.which = ctypes.cast(self._which, ctypes.c_void_p)
+            self.u_out = ctypes.cast(self._u_out, ctypes.c_void_p)
+            self.u_in = ctypes.cast(self._u_in, ctypes.c_void_p)
+
+    def run(self, stream_handle):
+        c = self.cfg.to_c()
+        dev = 1 if self.on_device else 0
+        if not self.distributed:
+            check(lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys), ctypes.byref(c), dev,
+                                             ctypes.c_void_p(stream_handle)))
+            return
+        check(lib().cdclq_prepare_factors(self.ins, len(self.ins), self.which, len(self.mine), ctypes.byref(c),
+                                          self.u_out, dev, ctypes.c_void_p(stream_handle)))
+        exchange_factors(self.u, self.owner)
+        check(lib().cdclq_quantize_batch_prepared(self.ins, len(self.ins), self.u_in, self.lys, len(self.lys),
+                                                  ctypes.byref(c), dev, ctypes.c_void_p(stream_handle)))

@@ -195,6 +195,7 @@ struct PrepEntry {
     float* h32 = nullptr;
     uint32_t* perm_dev = nullptr;
     bool owned = false;  // cudaMalloc'd (prep cache) rather than arena
+    bool ext_u = false;  // u supplied by the caller (prepared on another rank): only h32 is built here
     void release() {
         if (owned) {
             cudaFree(u);
@@ -296,6 +297,7 @@ struct LayerPlan {
 // Factorisation of a set of distinct inputs of one width (one batch of launches on its own stream).
 struct FactorGroup {
     size_t n = 0;
+    bool h32_only = false;          // U supplied by the caller: only the damped permuted Hessian is built
     std::vector<const float*> hs;   // device Hessians (original order)
     std::vector<PrepEntry*> es;     // receive damp_val; u/h32/perm_dev already allocated
     size_t b0 = 0, nb = 0;          // current sub-batch
@@ -307,7 +309,8 @@ struct FactorGroup {
     std::vector<double> damp;
 };
 
-static size_t factor_item_bytes(size_t n) {
+static size_t factor_item_bytes(size_t n, bool h32_only = false) {
+    if (h32_only) return n * sizeof(double) + 256;
     return 2 * n * n * sizeof(double) + 96 * n * sizeof(double) + n * sizeof(double) + 256;
 }
 
@@ -334,25 +337,30 @@ static int factor_launch(FactorGroup& g, const cdclq_config& cfg) {
     for (size_t i = 0; i < nb; i++) {
         PrepEntry* pe = g.es[g.b0 + i];
         PrepItem& it = items[i];
+        it = PrepItem{};
         it.h = g.hs[g.b0 + i];
         it.perm = pe->perm_dev;
-        if ((rc = ar.alloc(&it.hr, n * n))) return rc;
-        if ((rc = ar.alloc(&it.y, n * n))) return rc;
-        if ((rc = ar.alloc(&it.tbuf, 96 * n))) return rc;
+        if (!g.h32_only) {
+            if ((rc = ar.alloc(&it.hr, n * n))) return rc;
+            if ((rc = ar.alloc(&it.y, n * n))) return rc;
+            if ((rc = ar.alloc(&it.tbuf, 96 * n))) return rc;
+            it.u = pe->u;
+            CDCLQ_CUDA_TRY(cudaMemsetAsync(it.y, 0, n * n * sizeof(double), g.st));
+        }
         if ((rc = ar.alloc(&it.dg, n))) return rc;
         it.h32 = pe->h32;
-        it.u = pe->u;
         it.damp_val = g.damp_dev + i;
         it.status = g.status_dev + i;
-        CDCLQ_CUDA_TRY(cudaMemsetAsync(it.y, 0, n * n * sizeof(double), g.st));
     }
     PrepItem* items_dev = nullptr;
     if ((rc = ar.alloc(&items_dev, nb))) return rc;
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(items_dev, items.data(), sizeof(PrepItem) * nb, cudaMemcpyHostToDevice, g.st));
     if ((rc = launch_prepare(items_dev, (int)nb, (int)n, cfg.damp, g.st))) return rc;
-    if ((rc = launch_cholesky(items_dev, (int)nb, (int)n, g.st))) return rc;
-    if ((rc = launch_tri_inverse(items_dev, (int)nb, (int)n, g.st))) return rc;
-    if ((rc = launch_u_scatter(items_dev, (int)nb, (int)n, g.st))) return rc;
+    if (!g.h32_only) {
+        if ((rc = launch_cholesky(items_dev, (int)nb, (int)n, g.st))) return rc;
+        if ((rc = launch_tri_inverse(items_dev, (int)nb, (int)n, g.st))) return rc;
+        if ((rc = launch_u_scatter(items_dev, (int)nb, (int)n, g.st))) return rc;
+    }
     g.status.assign(nb, FactorStatus{0, -1, 0.0});
     g.damp.assign(nb, 0.0);
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(g.status.data(), g.status_dev, sizeof(FactorStatus) * nb, cudaMemcpyDeviceToHost, g.st));
@@ -378,13 +386,26 @@ static int factor_finish(FactorGroup& g) {
 // Factorise every group.  Groups of different widths are independent: when their work matrices fit in
 // free memory together they run concurrently on separate streams (the latency-bound panel steps of one
 // width overlap the other's); otherwise each group runs alone in memory-bounded sub-batches.
-static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config& cfg, cudaStream_t st) {
+static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config& cfg, cudaStream_t st,
+                            uint64_t* batches = nullptr) {
     if (groups.empty()) return 0;
     size_t freeb = 0, totalb = 0;
     cudaMemGetInfo(&freeb, &totalb);
+    {
+        // memory the stream-ordered pool keeps cached (released by this library's earlier calls) is free for
+        // the pool's next allocations, although the driver counts it as used
+        int dev = 0;
+        cudaMemPool_t pool;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+            uint64_t reserved = 0, used = 0;
+            if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &reserved) == cudaSuccess &&
+                cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &used) == cudaSuccess && reserved > used)
+                freeb += (size_t)(reserved - used);
+        }
+    }
     size_t budget = freeb > ((size_t)4 << 30) ? freeb - ((size_t)4 << 30) : freeb / 2;
     size_t need = 0;
-    for (auto& g : groups) need += factor_item_bytes(g.n) * g.hs.size();
+    for (auto& g : groups) need += factor_item_bytes(g.n, g.h32_only) * g.hs.size();
     cudaEvent_t ready = nullptr;
     CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
     cudaEventRecord(ready, st);  // inputs uploaded / permutations copied on `st`
@@ -395,6 +416,7 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
     }
     cudaEventDestroy(ready);
     if (need <= budget) {
+        if (batches) *batches += groups.size();
         for (auto& g : groups) {
             g.b0 = 0;
             g.nb = g.hs.size();
@@ -407,9 +429,10 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
         return rc;
     }
     for (auto& g : groups) {
-        size_t max_items = std::max<size_t>(1, budget / factor_item_bytes(g.n));
+        size_t max_items = std::max<size_t>(1, budget / factor_item_bytes(g.n, g.h32_only));
         for (g.b0 = 0; g.b0 < g.hs.size(); g.b0 += max_items) {
             g.nb = std::min(max_items, g.hs.size() - g.b0);
+            if (batches) *batches += 1;
             if ((rc = factor_launch(g, cfg))) return rc;
             if ((rc = factor_finish(g))) return rc;
         }
@@ -419,7 +442,8 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
 
 // The whole path for a batch of layers.  `cache` (single-layer calls only) is the one-entry memo.
 static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>& layers, const cdclq_config& cfg,
-               bool on_device, cudaStream_t st, cdclq_prep_cache* cache, const std::string& hkey) {
+               bool on_device, cudaStream_t st, cdclq_prep_cache* cache, const std::string& hkey,
+               const float* const* u_ext = nullptr) {
     const double t_start = now_s();
     const uint64_t launches0 = g_launches.load();
     PhaseEvents pev;
@@ -523,6 +547,9 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             PrepEntry pe;
             pe.n = P.n;
             pe.perm = P.perm;
+            // a caller-supplied factor stands for the input's W-independent permutation only
+            pe.ext_u = u_ext && u_ext[layers[li].input] && P.nskel == 0 &&
+                       !(cfg.skeleton_pct > 0.0 && P.g < P.n);
             preps.push_back(pe);
             prep_input.push_back(layers[li].input);
             found = (int)preps.size() - 1;
@@ -534,11 +561,15 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         cache->e.release();
     }
     // allocate factors and upload Hessians that are needed
-    std::map<size_t, std::vector<size_t>> by_n;
+    std::map<size_t, std::vector<size_t>> by_n, by_n_h32;
     for (size_t k = 0; k < preps.size(); k++) {
         PrepEntry& pe = preps[k];
         size_t n = pe.n;
-        if (cache) {
+        if (pe.ext_u) {
+            pe.u = const_cast<float*>(u_ext[prep_input[k]]);
+            if ((rc = ar.alloc(&pe.h32, n * n))) return rc;
+            if ((rc = ar.alloc(&pe.perm_dev, n))) return rc;
+        } else if (cache) {
             CDCLQ_CUDA_TRY(cudaMalloc(&pe.u, n * n * sizeof(float)));
             CDCLQ_CUDA_TRY(cudaMalloc(&pe.h32, n * n * sizeof(float)));
             CDCLQ_CUDA_TRY(cudaMalloc(&pe.perm_dev, n * sizeof(uint32_t)));
@@ -560,19 +591,23 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
                 h_dev[in] = hd;
             }
         }
-        by_n[n].push_back(k);
+        (pe.ext_u ? by_n_h32 : by_n)[n].push_back(k);
     }
     std::vector<FactorGroup> groups;
-    for (auto& kv : by_n) {
-        FactorGroup g;
-        g.n = kv.first;
-        for (size_t k : kv.second) {
-            g.hs.push_back(h_dev[prep_input[k]]);
-            g.es.push_back(&preps[k]);
+    for (int pass = 0; pass < 2; pass++) {
+        for (auto& kv : (pass == 0 ? by_n : by_n_h32)) {
+            FactorGroup g;
+            g.n = kv.first;
+            g.h32_only = pass == 1;
+            for (size_t k : kv.second) {
+                g.hs.push_back(h_dev[prep_input[k]]);
+                g.es.push_back(&preps[k]);
+            }
+            groups.push_back(std::move(g));
         }
-        groups.push_back(std::move(g));
     }
-    if ((rc = factorize_groups(groups, cfg, st))) {
+    uint64_t factor_batches = 0;
+    if ((rc = factorize_groups(groups, cfg, st, &factor_batches))) {
         if (cache) {
             for (auto& pe : preps) pe.release();
         }
@@ -786,9 +821,30 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         int* counter = nullptr;
         if ((rc = ar.alloc(&counter, 1))) return rc;
         const int g0 = (int)plans[0].g, sbw0 = (int)std::min<size_t>(cfg.sub_block, maxn);
-        const int bm = repair_tile_rows(g0, sbw0, (int)max_rows);
+        int bm = repair_tile_rows(g0, sbw0, (int)max_rows);
         // chunks of more than one row tile: a 2-CTA cluster per chunk
-        if (max_rows > (size_t)bm && max_rows <= (size_t)bm * RP_MAX_TILES_PER_CHUNK)
+        bool cluster = max_rows > (size_t)bm && max_rows <= (size_t)bm * RP_MAX_TILES_PER_CHUNK;
+        if (!cluster && bm == 128) {
+            // One CTA per 128-row chunk is the efficient GEMM shape, but a chunk's passes then run on one SM:
+            // when the heaviest chunk alone outlasts the average load of a CTA slot (few chunks per slot, as in
+            // one GPU's row shard of a model), its rows go to a 2-CTA cluster of 64-row tiles instead.  Chunk
+            // work ~ rows x n^2 per pass; 64-row tiles run the GEMMs about 13% slower.
+            double total_w = 0.0, max_w = 0.0;
+            for (auto& P : plans)
+                for (size_t c = 0; c < P.nchunks; c++) {
+                    const double w = (double)std::min(P.rc, P.d_out - c * P.rc) * (double)P.n * (double)P.n;
+                    total_w += w;
+                    max_w = std::max(max_w, w);
+                }
+            const double slots = 2.0 * sms;
+            const double t_single = std::max(total_w / slots, max_w);
+            const double t_pair = std::max(total_w / slots, 0.5 * max_w) / 0.87;
+            if (t_pair < t_single) {
+                bm = 64;
+                cluster = true;
+            }
+        }
+        if (cluster)
             rc = launch_repair_cluster(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);
         else
             rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);
@@ -874,6 +930,8 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             pf.factorisations++;
         }
         pf.launches = g_launches.load() - launches0;
+        pf.factor_batches = factor_batches;
+        pf.ms_host = (now_s() - t_start) * 1e3;
     }
 
     // ---- statistics, summed over chunks in order (src/engine.rs:786-797)
@@ -1024,8 +1082,9 @@ int cdclq_quantize_layer(const float* w, size_t d_out, size_t d_in, const float*
                                    zeros_out, stats_out, nullptr);
 }
 
-int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
-                         size_t n_layers, const cdclq_config* cfg, int on_device, void* stream) {
+static int quantize_batch_impl(const cdclq_batch_input* inputs, size_t n_inputs, const float* const* u_in,
+                               const cdclq_batch_layer* layers, size_t n_layers, const cdclq_config* cfg, int on_device,
+                               void* stream) {
     if (!cfg || (!inputs && n_inputs) || (!layers && n_layers)) return set_error(CDCLQ_ERR_ARG, "null argument");
     int rc = ensure_device();
     if (rc) return rc;
@@ -1059,13 +1118,91 @@ int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const
         std::map<size_t, std::vector<LayerReq>> by_g;
         for (auto& L : v) by_g[effective_group(*cfg, in[L.input].n)].push_back(L);
         for (auto& kv : by_g) {
-            int r = run(in, kv.second, *cfg, on_device != 0, st, nullptr, "");
+            int r = run(in, kv.second, *cfg, on_device != 0, st, nullptr, "", u_in);
             if (r) return r;
         }
         return 0;
     };
     if ((rc = run_groups(small))) return rc;
     return run_groups(large);
+}
+
+int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
+                         size_t n_layers, const cdclq_config* cfg, int on_device, void* stream) {
+    return quantize_batch_impl(inputs, n_inputs, nullptr, layers, n_layers, cfg, on_device, stream);
+}
+
+int cdclq_quantize_batch_prepared(const cdclq_batch_input* inputs, size_t n_inputs, const float* const* u_in,
+                                  const cdclq_batch_layer* layers, size_t n_layers, const cdclq_config* cfg,
+                                  int on_device, void* stream) {
+    if (!u_in) return set_error(CDCLQ_ERR_ARG, "null argument");
+    if (cfg && cfg->skeleton_pct > 0.0)
+        return set_error(CDCLQ_ERR_CONFIG, "prepared factors need a W-independent permutation (skeleton_pct = 0)");
+    return quantize_batch_impl(inputs, n_inputs, u_in, layers, n_layers, cfg, on_device, stream);
+}
+
+int cdclq_prepare_factors(const cdclq_batch_input* inputs, size_t n_inputs, const size_t* which, size_t n_which,
+                          const cdclq_config* cfg, float* const* u_out, int on_device, void* stream) {
+    if (!cfg || (!inputs && n_inputs) || (!which && n_which) || (!u_out && n_which))
+        return set_error(CDCLQ_ERR_ARG, "null argument");
+    if (cfg->skeleton_pct > 0.0)
+        return set_error(CDCLQ_ERR_CONFIG, "prepared factors need a W-independent permutation (skeleton_pct = 0)");
+    int rc = ensure_device();
+    if (rc) return rc;
+    if (n_which == 0) return CDCLQ_OK;
+    cudaStream_t st = stream ? (cudaStream_t)stream : (on_device ? (cudaStream_t)0 : lib_stream());
+    Arena ar(st);
+    std::vector<PrepEntry> preps(n_which);
+    std::vector<const float*> h_dev(n_which, nullptr);
+    std::map<size_t, std::vector<size_t>> by_n;
+    for (size_t k = 0; k < n_which; k++) {
+        const size_t i = which[k];
+        if (i >= n_inputs) return set_error(CDCLQ_ERR_ARG, "input index out of range");
+        const size_t n = inputs[i].n;
+        if (n == 0 || !inputs[i].h || !u_out[k]) return set_error(CDCLQ_ERR_ARG, "null argument");
+        if ((rc = validate(*cfg, n))) return rc;
+        if ((rc = check_tiling(*cfg, n))) return rc;
+        // act-order (or natural) permutation from the raw diagonal (src/engine.rs:271-304, no skeleton)
+        std::vector<double> hdiag(n);
+        if (on_device) {
+            double* dg = nullptr;
+            if ((rc = ar.alloc(&dg, n))) return rc;
+            if ((rc = launch_hdiag(inputs[i].h, (int)n, dg, st))) return rc;
+            CDCLQ_CUDA_TRY(cudaMemcpyAsync(hdiag.data(), dg, n * sizeof(double), cudaMemcpyDeviceToHost, st));
+            CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+            ar.free_one(dg);
+            h_dev[k] = inputs[i].h;
+        } else {
+            for (size_t j = 0; j < n; j++) hdiag[j] = (double)inputs[i].h[j * n + j];
+            float* hd = nullptr;
+            if ((rc = ar.alloc(&hd, n * n))) return rc;
+            CDCLQ_CUDA_TRY(cudaMemcpyAsync(hd, inputs[i].h, n * n * sizeof(float), cudaMemcpyHostToDevice, st));
+            h_dev[k] = hd;
+        }
+        PrepEntry& pe = preps[k];
+        size_t nskel = 0;
+        compute_perm(hdiag, nullptr, n, effective_group(*cfg, n), *cfg, pe.perm, nskel);
+        pe.n = n;
+        pe.u = u_out[k];
+        pe.h32 = nullptr;  // only U is wanted: the quantizing ranks rebuild the damped Hessian themselves
+        if ((rc = ar.alloc(&pe.perm_dev, n))) return rc;
+        CDCLQ_CUDA_TRY(cudaMemcpyAsync(pe.perm_dev, pe.perm.data(), n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+        by_n[n].push_back(k);
+    }
+    std::vector<FactorGroup> groups;
+    for (auto& kv : by_n) {
+        FactorGroup g;
+        g.n = kv.first;
+        for (size_t k : kv.second) {
+            g.hs.push_back(h_dev[k]);
+            g.es.push_back(&preps[k]);
+        }
+        groups.push_back(std::move(g));
+    }
+    // factorize_groups waits on the host for every factor stream: the factors are complete on return
+    rc = factorize_groups(groups, *cfg, st);
+    if (!rc) CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+    return rc;
 }
 
 // ---- linalg entry points (host buffers) -------------------------------------------------------------------

@@ -17,10 +17,10 @@ namespace cdclq {
 struct PrepItem {
     const float* h;         // n x n f32, original column order
     const uint32_t* perm;   // n, permuted position -> original column
-    double* hr;             // n x n f64: flipped damped permuted Hessian, then L in its lower triangle
+    double* hr;             // n x n f64: flipped damped permuted Hessian, then L in its lower triangle (or null)
     double* y;              // n x n f64: L^-1 (lower)
     double* tbuf;           // 96 x n f64 scratch of the triangular inverse
-    float* h32;             // n x n f32 damped permuted Hessian (phase 2 metric)
+    float* h32;             // n x n f32 damped permuted Hessian (phase 2 metric, or null)
     float* u;               // n x n f32 upper factor, H^-1 = U^T U (phase 1)
     double* dg;             // n f64 scratch: patched diagonal
     double* damp_val;       // 1 f64 out

@@ -49,7 +49,8 @@ __global__ void prep_mean_kernel(const PrepItem* __restrict__ items, int n, doub
     it.status->value = 0.0;
 }
 
-// hp[a][b] = (f64) h[perm a][perm b], diagonal patched and damped; h32 = (f32) hp; hr = flip(hp)
+// hp[a][b] = (f64) h[perm a][perm b], diagonal patched and damped; h32 = (f32) hp; hr = flip(hp).  Either
+// output may be absent (null): h32 alone when the factor U comes from elsewhere, hr alone when only U is wanted.
 __global__ void prep_fill_kernel(const PrepItem* __restrict__ items, int n) {
     const PrepItem it = items[blockIdx.z];
     int a = blockIdx.y;
@@ -60,8 +61,8 @@ __global__ void prep_fill_kernel(const PrepItem* __restrict__ items, int n) {
         v = __dadd_rn(it.dg[a], *it.damp_val);
     else
         v = (double)it.h[(int64_t)it.perm[a] * n + it.perm[b]];
-    it.h32[(int64_t)a * n + b] = (float)v;
-    it.hr[(int64_t)(n - 1 - a) * n + (n - 1 - b)] = v;
+    if (it.h32) it.h32[(int64_t)a * n + b] = (float)v;
+    if (it.hr) it.hr[(int64_t)(n - 1 - a) * n + (n - 1 - b)] = v;
 }
 
 int launch_prepare(const PrepItem* items_dev, int nitems, int n, double damp, cudaStream_t st) {

@@ -153,6 +153,24 @@ typedef struct cdclq_batch_layer {
 int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
                          size_t n_layers, const cdclq_config* cfg, int on_device, void* stream);
 
+/* ---- multi-GPU: factorisations spread over ranks (the "compute once on the owning GPU, then broadcast"
+ * option for Prepared's U, src/engine.rs:320-342; the reference itself runs on one host) ----------------- */
+
+/* Upper factor U (H^-1 = U^T U of the damped Hessian, permuted order, src/linalg.rs:362-375) of the inputs
+ * listed in `which`, written to the caller's DEVICE buffers u_out[k] (n x n f32 each).  The permutation is
+ * the W-independent one (act-order or natural), so skeleton_pct must be 0.  `on_device` says where the
+ * Hessians live.  A rank factorises its share, then the factors are broadcast (NCCL) to every rank. */
+int cdclq_prepare_factors(const cdclq_batch_input* inputs, size_t n_inputs, const size_t* which, size_t n_which,
+                          const cdclq_config* cfg, float* const* u_out, int on_device, void* stream);
+
+/* cdclq_quantize_batch with the factorisation replaced by caller-supplied factors: u_in[i] is a DEVICE
+ * n x n f32 buffer produced by cdclq_prepare_factors for input i (on any rank, same configuration), or NULL
+ * to factorise that input here.  Only the damped permuted Hessian is rebuilt locally.  Results are identical
+ * to cdclq_quantize_batch.  skeleton_pct must be 0. */
+int cdclq_quantize_batch_prepared(const cdclq_batch_input* inputs, size_t n_inputs, const float* const* u_in,
+                                  const cdclq_batch_layer* layers, size_t n_layers, const cdclq_config* cfg,
+                                  int on_device, void* stream);
+
 /* ---- linear-algebra kernels (linalg.rs) ------------------------------------------------------------ */
 
 /* cholesky_lower (src/linalg.rs:200-276): in place on a host n x n f64 matrix; lower triangle = L. */
@@ -221,6 +239,8 @@ typedef struct cdclq_run_profile {
     uint64_t factorisations;
     uint64_t weights;
     uint64_t launches;      /* kernel launches issued by the call */
+    uint64_t factor_batches; /* factorisation launch batches: one per width when all fit in free memory */
+    double ms_host;         /* host wall time of the call */
 } cdclq_run_profile;
 
 int cdclq_last_run_profile(cdclq_run_profile* out);

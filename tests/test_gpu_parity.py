@@ -73,9 +73,17 @@ CASES = [
     ("group_512_refit", 32, 1024, 2500, 37, Config(group=512, block=128, sub_block=64, row_chunk=32, passes=2)),
     # >= 2 x SM-count row chunks: the persistent repair kernel (all passes of a chunk in one CTA)
     ("persistent_many_chunks", 2400, 96, 500, 38, Config(group=32, block=32, sub_block=16, row_chunk=8, passes=4)),
-    # chunks of more than 64 rows: a 2-CTA cluster per chunk (2 tiles, then 4 tiles split over the two CTAs)
-    ("cluster_rc100_ragged", 30100, 64, 400, 39, Config(group=32, block=64, sub_block=32, row_chunk=100, passes=3)),
-    ("cluster_rc200_4tiles", 30000, 48, 300, 40, Config(group=16, block=16, sub_block=16, row_chunk=200, passes=3)),
+    # 301 chunks of up to 100 rows: one CTA per chunk on 128-row tiles
+    ("persistent_rc100_ragged", 30100, 64, 400, 39, Config(group=32, block=64, sub_block=32, row_chunk=100,
+                                                           passes=3)),
+    # 200-row chunks = two 128-row tiles: a 2-CTA cluster per chunk
+    ("cluster_rc200_2tiles", 30000, 48, 300, 40, Config(group=16, block=16, sub_block=16, row_chunk=200, passes=3)),
+    # 150 chunks of 128 rows on 296 CTA slots: each chunk's rows split over a 2-CTA cluster of 64-row tiles
+    ("cluster_pairs_few_chunks", 19200, 64, 400, 44, Config(group=32, block=64, sub_block=32, row_chunk=128,
+                                                            passes=3)),
+    # 1200-row chunks = ten 128-row tiles (ragged last tile) split over a cluster
+    ("cluster_rc1200_10tiles", 180000, 16, 200, 45, Config(group=8, block=8, sub_block=8, row_chunk=1200,
+                                                           passes=2)),
 ]
 
 

@@ -1,0 +1,120 @@
+"""Host logic of the multi-GPU path (cdclq.pipeline) without a GPU: row shards, the factorisation owners,
+the factor exchange over a world-size-2 gloo process group, and the prepared-factor entry points' argument
+checks."""
+import ctypes
+import os
+import socket
+
+
+from conftest import ROOT
+
+TINYLLAMA_INPUTS = [2048, 2048, 2048, 5632] * 22
+
+
+def test_shard_rows_cover_every_row_in_whole_chunks():
+    from cdclq.pipeline import shard_rows
+
+    for d_out in (1, 64, 127, 128, 129, 256, 1000, 2048, 5632):
+        for rc in (16, 100, 128):
+            for world in (1, 2, 3, 4, 8):
+                spans = [shard_rows(d_out, rc, r, world) for r in range(world)]
+                assert spans[0][0] == 0 and spans[-1][1] == d_out
+                for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+                    assert a1 == b0  # contiguous, in rank order
+                for r0, r1 in spans:
+                    assert r0 <= r1
+                    assert r0 % rc == 0  # a shard starts on a row-chunk boundary
+                    assert r1 % rc == 0 or r1 == d_out
+
+
+def test_factorisation_owners_balance_n_cubed():
+    from cdclq.pipeline import assign_factorisations
+
+    ns = TINYLLAMA_INPUTS
+    for world in (1, 2, 4, 8):
+        owner = assign_factorisations(ns, world)
+        assert owner == assign_factorisations(ns, world)  # deterministic: every rank derives the same table
+        assert set(owner) == set(range(world))
+        load = [sum(float(n) ** 3 for n, o in zip(ns, owner) if o == r) for r in range(world)]
+        # LPT bound: no rank above the mean by more than the largest single job
+        assert max(load) <= sum(load) / world + 5632.0 ** 3 + 1.0
+    # the 22 widest inputs (the down projections) are spread first, one per rank in turn
+    owner = assign_factorisations(ns, 8)
+    down = [owner[i] for i in range(3, len(ns), 4)]
+    assert sorted(down[:8]) == list(range(8))
+
+
+def test_prepared_entry_points_reject_a_weight_dependent_permutation():
+    import cdclq
+    from cdclq.abi import CBatchInput, Config
+
+    L = cdclq.lib()
+    c = Config(skeleton_pct=2.0).to_c()
+    ins = (CBatchInput * 1)()
+    ins[0].n = 64
+    u = (ctypes.c_void_p * 1)(None)
+    which = (ctypes.c_size_t * 1)(0)
+    rc = L.cdclq_prepare_factors(ins, 1, ctypes.cast(which, ctypes.c_void_p), 1, ctypes.byref(c),
+                                 ctypes.cast(u, ctypes.c_void_p), 1, None)
+    assert rc == -1  # CDCLQ_ERR_CONFIG
+    assert L.cdclq_last_error().decode() == "prepared factors need a W-independent permutation (skeleton_pct = 0)"
+    rc = L.cdclq_quantize_batch_prepared(ins, 1, ctypes.cast(u, ctypes.c_void_p), None, 0, ctypes.byref(c), 1, None)
+    assert rc == -1
+    rc = L.cdclq_quantize_batch_prepared(ins, 1, None, None, 0, ctypes.byref(Config().to_c()), 1, None)
+    assert rc == -3 and L.cdclq_last_error().decode() == "null argument"  # CDCLQ_ERR_ARG
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _exchange_worker(rank, world, port, q):
+    import sys
+
+    sys.path.insert(0, os.path.join(ROOT, "cdcl-gptq_b200"))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from cdclq.pipeline import assign_factorisations, exchange_factors
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        ns = [8, 16, 8, 24, 16]
+        owner = assign_factorisations(ns, world)
+        # each rank fills only the factors it owns; the others hold garbage before the exchange
+        fac = []
+        for i, n in enumerate(ns):
+            t = torch.full((n, n), -1.0)
+            if owner[i] == rank:
+                t = torch.arange(n * n, dtype=torch.float32).reshape(n, n) + 1000.0 * i
+            fac.append(t)
+        exchange_factors(fac, owner)
+        ok = all(torch.equal(t, torch.arange(n * n, dtype=torch.float32).reshape(n, n) + 1000.0 * i)
+                 for i, (t, n) in enumerate(zip(fac, ns)))
+        q.put((rank, ok, owner))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_factor_exchange_two_ranks_gloo():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort()
+    assert all(ok for _, ok, _ in res)
+    assert res[0][2] == res[1][2]  # both ranks derived the same owners
