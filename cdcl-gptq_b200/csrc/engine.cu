@@ -270,6 +270,12 @@ static cudaStream_t lib_stream() {
     return s;
 }
 
+static cudaStream_t copy_stream() {
+    static thread_local cudaStream_t s = nullptr;
+    if (!s) cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    return s;
+}
+
 static double now_s() {
     return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
@@ -297,6 +303,8 @@ struct LayerPlan {
 // Factorisation of a set of distinct inputs of one width (one batch of launches on its own stream).
 struct FactorGroup {
     size_t n = 0;
+    std::vector<size_t> inputs;     // input index of each item
+    cudaEvent_t ready = nullptr;    // its Hessians are on the device (null: everything issued so far on `st`)
     bool h32_only = false;          // U supplied by the caller: only the damped permuted Hessian is built
     std::vector<const float*> hs;   // device Hessians (original order)
     std::vector<PrepEntry*> es;     // receive damp_val; u/h32/perm_dev already allocated
@@ -412,7 +420,11 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
     int rc = 0;
     for (size_t k = 0; k < groups.size(); k++) {
         groups[k].st = pool_stream(k);
-        cudaStreamWaitEvent(groups[k].st, ready, 0);
+        cudaStreamWaitEvent(groups[k].st, groups[k].ready ? groups[k].ready : ready, 0);
+        if (groups[k].ready) {
+            cudaEventDestroy(groups[k].ready);
+            groups[k].ready = nullptr;
+        }
     }
     cudaEventDestroy(ready);
     if (need <= budget) {
@@ -484,6 +496,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
 
     // ---- weights on the device, permutations
     std::vector<LayerPlan> plans(layers.size());
+    std::vector<size_t> w_uploads;  // host weights copied behind the Hessians
     std::vector<std::vector<uint32_t>> input_perm(nin);  // cache of the W-independent permutation
     std::vector<char> input_perm_done(nin, 0);
     for (size_t li = 0; li < layers.size(); li++) {
@@ -493,15 +506,18 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         P.n = inputs[L.input].n;
         P.g = effective_group(cfg, P.n);
         P.ng = (P.n + P.g - 1) / P.g;
+        const bool skel = cfg.skeleton_pct > 0.0 && P.g < P.n;
         if (on_device) {
             P.w_dev = L.w;
         } else {
             float* wd = nullptr;
             if ((rc = ar.alloc(&wd, P.d_out * P.n))) return rc;
-            CDCLQ_CUDA_TRY(cudaMemcpyAsync(wd, L.w, P.d_out * P.n * sizeof(float), cudaMemcpyHostToDevice, st));
             P.w_dev = wd;
+            if (skel)  // the skeleton ranks columns by W: upload now
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(wd, L.w, P.d_out * P.n * sizeof(float), cudaMemcpyHostToDevice, st));
+            else  // uploaded on the copy stream while the factorisations run
+                w_uploads.push_back(li);
         }
-        const bool skel = cfg.skeleton_pct > 0.0 && P.g < P.n;
         if (skel) {
             double* cs_dev = nullptr;
             if ((rc = ar.alloc(&cs_dev, P.n))) return rc;
@@ -585,9 +601,8 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             if (on_device) {
                 h_dev[in] = inputs[in].h;
             } else {
-                float* hd = nullptr;
+                float* hd = nullptr;  // uploaded below, group by group
                 if ((rc = ar.alloc(&hd, n * n))) return rc;
-                CDCLQ_CUDA_TRY(cudaMemcpyAsync(hd, inputs[in].h, n * n * sizeof(float), cudaMemcpyHostToDevice, st));
                 h_dev[in] = hd;
             }
         }
@@ -595,19 +610,61 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     }
     std::vector<FactorGroup> groups;
     for (int pass = 0; pass < 2; pass++) {
-        for (auto& kv : (pass == 0 ? by_n : by_n_h32)) {
+        auto& m = pass == 0 ? by_n : by_n_h32;
+        for (auto it = m.rbegin(); it != m.rend(); ++it) {  // widest first: the longest factorisations
+            auto& kv = *it;
             FactorGroup g;
             g.n = kv.first;
             g.h32_only = pass == 1;
             for (size_t k : kv.second) {
                 g.hs.push_back(h_dev[prep_input[k]]);
                 g.es.push_back(&preps[k]);
+                g.inputs.push_back(prep_input[k]);
             }
             groups.push_back(std::move(g));
         }
     }
+    // Host Hessians: uploaded group by group (widest first) so that each group's factorisation starts as soon
+    // as its own inputs have arrived.
+    if (!on_device) {
+        std::vector<char> sent(nin, 0);
+        for (auto& g : groups) {
+            for (size_t i = 0; i < g.hs.size(); i++) {
+                const size_t in = g.inputs[i];
+                if (sent[in]) continue;
+                sent[in] = 1;
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(const_cast<float*>(h_dev[in]), inputs[in].h, g.n * g.n * sizeof(float),
+                                               cudaMemcpyHostToDevice, st));
+            }
+            CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&g.ready, cudaEventDisableTiming));
+            cudaEventRecord(g.ready, st);
+        }
+    }
+    // Host weights: copied on a second stream after the Hessians (which the factorisations need first), so the
+    // transfer overlaps the factorisations; `st` waits for it before the weights are permuted.
+    cudaEvent_t w_ready = nullptr;
+    if (!w_uploads.empty()) {
+        cudaStream_t cs = copy_stream();
+        cudaEvent_t h_done = nullptr;
+        CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&h_done, cudaEventDisableTiming));
+        CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&w_ready, cudaEventDisableTiming));
+        cudaEventRecord(h_done, st);
+        cudaStreamWaitEvent(cs, h_done, 0);
+        cudaEventDestroy(h_done);
+        for (size_t li : w_uploads) {
+            const LayerPlan& P = plans[li];
+            CDCLQ_CUDA_TRY(cudaMemcpyAsync(const_cast<float*>(P.w_dev), layers[li].w, P.d_out * P.n * sizeof(float),
+                                           cudaMemcpyHostToDevice, cs));
+        }
+        cudaEventRecord(w_ready, cs);
+    }
     uint64_t factor_batches = 0;
-    if ((rc = factorize_groups(groups, cfg, st, &factor_batches))) {
+    rc = factorize_groups(groups, cfg, st, &factor_batches);
+    if (w_ready) {
+        cudaStreamWaitEvent(st, w_ready, 0);
+        cudaEventDestroy(w_ready);
+    }
+    if (rc) {
         if (cache) {
             for (auto& pe : preps) pe.release();
         }
