@@ -285,6 +285,20 @@ def run_reference_arm(args, torch, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def repair_traffic_bytes(weights):
+    """DRAM bytes of one repair launch for `weights` weights, from the committed ncu summary of the repair
+    kernel (dram__bytes_read.sum + dram__bytes_write.sum per weight of a captured smaller case, scaled by
+    weights); None when the summary is absent."""
+    path = os.path.join(ROOT, "profiles", "repair_persistent_kernel_2layers.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_weight:"):
+                return float(line.split(":", 1)[1]) * weights
+    except OSError:
+        pass
+    return None
+
+
 def workload_config(cfg):
     return {"workload": "TinyLlama-1.1B-shaped model (configs[1]): 22 decoder layers, 154 linear layers, "
                         "9.69e8 bf16-valued weights, 88 Hessians from 262144 seeded tokens",
@@ -415,7 +429,9 @@ def main():
                 "kernel": "repair_persistent_kernel (CDCL repair: block gradients on the FP32 SIMT GEMM core, "
                           "per-row refit and coordinate descent)",
                 "bound": "fp32", "achieved": rep_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
-                "frac": rep_tflops / fp32_peak if fp32_peak else None, "traffic": None,
+                "frac": rep_tflops / fp32_peak if fp32_peak else None,
+                "traffic": repair_traffic_bytes(prof["weights"]),
+                "traffic_source": "profiles/repair_persistent_kernel_2layers.md (ncu DRAM bytes per weight, scaled)",
                 "peak_source": "measured in this run: cuBLAS SGEMM 8192^3 with TF32 off (FFMA); MEASURED_PEAKS.json "
                                "has no FP32 CUDA-core figure",
             },

@@ -25,6 +25,12 @@ struct RepairTiles {
     static constexpr int LD = BM + 4;    // [col][row] GEMM result tiles (16-byte aligned rows)
     static constexpr int CSLD = BM + 4;  // [col][row] code tiles, bytes: consecutive columns start in distinct banks
     static constexpr int LDW = BM + 1;   // [col][row] W_hat tile: consecutive columns start in distinct banks
+    // Coordinate descent: P = 256 / BM threads share a row, thread h updating gradient columns h, h + P, ...;
+    // the gradient tile's column stride LDG = BM + BM/8 (= 32/P mod 32) puts the P threads of a row in
+    // distinct banks.
+    static constexpr int P = GEMM_THREADS / BM;
+    static constexpr int LDG = BM + BM / 8;
+    static_assert(LDG % 4 == 0 && (LDG % 32) * P == 32, "gradient stride");
     static constexpr int STAGE_FLOATS = W128::STAGE_FLOATS > W64::STAGE_FLOATS
                                             ? (W128::STAGE_FLOATS > W32::STAGE_FLOATS ? W128::STAGE_FLOATS
                                                                                       : W32::STAGE_FLOATS)
@@ -89,7 +95,7 @@ struct AFromCodes {
 
 template <class S, class AM>
 __device__ __forceinline__ void gemm_to_tile_s(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd,
-                                               int K, float* out, float* stage) {
+                                               int K, float* out, int ldo, float* stage) {
     int ty, tx;
     gemm_coords(threadIdx.x, ty, tx);
     float acc[S::TM][S::TN];
@@ -106,24 +112,24 @@ __device__ __forceinline__ void gemm_to_tile_s(const AM& am, const float* b, int
         if (cc < wd) {
 #pragma unroll
             for (int v = 0; v < S::TM / 4; v++)
-                *reinterpret_cast<float4*>(out + cc * S::ALD + TileMap<S>::row(ty, 4 * v)) =
+                *reinterpret_cast<float4*>(out + cc * ldo + TileMap<S>::row(ty, 4 * v)) =
                     make_float4(acc[4 * v][j], acc[4 * v + 1][j], acc[4 * v + 2][j], acc[4 * v + 3][j]);
         }
     }
 }
 
-// out[c][row] = (A B)[row][c] for c < wd (wd <= 128), B = b[k][col0 + c], via the narrowest fitting tile.
-// Ends synchronised.
+// out[c * ldo + row] = (A B)[row][c] for c < wd (wd <= 128), B = b[k][col0 + c], via the narrowest fitting
+// tile; ldo is a multiple of 4.  Ends synchronised.
 template <int BM, class AM>
 __device__ void gemm_to_tile(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
-                             float* stage) {
+                             int ldo, float* stage) {
     using RT = RepairTiles<BM>;
     if (wd > 64)
-        gemm_to_tile_s<typename RT::W128>(am, b, ldb, col0, wd, K, out, stage);
+        gemm_to_tile_s<typename RT::W128>(am, b, ldb, col0, wd, K, out, ldo, stage);
     else if (wd > 32)
-        gemm_to_tile_s<typename RT::W64>(am, b, ldb, col0, wd, K, out, stage);
+        gemm_to_tile_s<typename RT::W64>(am, b, ldb, col0, wd, K, out, ldo, stage);
     else
-        gemm_to_tile_s<typename RT::W32>(am, b, ldb, col0, wd, K, out, stage);
+        gemm_to_tile_s<typename RT::W32>(am, b, ldb, col0, wd, K, out, ldo, stage);
     __syncthreads();
 }
 
@@ -209,7 +215,7 @@ static __host__ __device__ inline RepairLayout repair_layout(int g, int sbw) {
     L.refit_tile = al16(gcap * CSLD);
     size_t refit = L.refit_tile + al16((size_t)128 * LD * 4);
     L.cd_gt = al16((size_t)sbw * CSLD);
-    size_t gt_bytes = al16((size_t)sbw * LD * 4);
+    size_t gt_bytes = al16((size_t)sbw * RepairTiles<BM>::LDG * 4);
     if (sbw <= 128) {  // one GEMM tile: staging inside the gradient tile
         L.cd_stage = L.cd_gt;
         L.cd_wqs = L.cd_gt + (gt_bytes > STAGE ? gt_bytes : al16(STAGE));
@@ -288,7 +294,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             tile, tile);
+                             tile, LD, tile);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
@@ -302,7 +308,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
-                             wt, wd, tile, tile);
+                             wt, wd, tile, LD, tile);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
@@ -347,17 +353,28 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
 template <int BM>
 __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
                         unsigned long long& my_upd) {
-    constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    constexpr int LD = RepairTiles<BM>::LDG, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
+    constexpr int P = RepairTiles<BM>::P;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
     float* E = ci.e + (int64_t)r0 * n;
     float* WQ = ci.wq + (int64_t)r0 * n;
     uint8_t* CODES = ci.codes + (int64_t)r0 * n;
+    // sweep layout: P consecutive lanes share row r; lane h of the group owns gradient columns h, h+P, ...
+    const int lane = tid & 31;
+    const int r = (tid >> 5) * (32 / P) + lane / P, h = lane % P;
+    const unsigned pmask = ((1u << P) - 1u) << (lane & ~(P - 1));
+    // the row's loss bookkeeping moves to shared memory while the sweep threads own the rows
+    __syncthreads();
+    if (tid < BM) {
+        sm.rowdelta[tid] = my_delta;
+        sm.rowupd[tid] = my_upd;
+    }
     const float* SC = ci.scales + (int64_t)r0 * ng;
     const float* ZR = ci.zeros + (int64_t)r0 * ng;
     const float* H = ci.h;
     const int n_sel = ci.st->n_sel;
     uint8_t* cs = sm.body;     // [sbw][CSLD]
-    float* gt = sm.cd_gt;      // [sbw][LD] block gradient
+    float* gt = sm.cd_gt;      // [sbw][LDG] block gradient
     float* wqs = sm.cd_wqs;    // [sbw][LDW] W_hat
     float* hss = sm.cd_hss;    // [sbw][sbw] or its diagonal
     const bool hss_full = (size_t)sbw * sbw * 4 <= (size_t)HSS_MAX_BYTES;
@@ -376,10 +393,13 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
             gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             gt + (size_t)t0 * LD, sm.cd_stage);
+                             gt + (size_t)t0 * LD, LD, sm.cd_stage);
         }
-        if (tid < rs) {
-            const int r = tid;
+        if (r < rs) {
+            // The P threads of a row take every decision together (identical inputs, identical results) and
+            // split each rank-1 gradient update; thread h = 0 writes the row's state and keeps its bookkeeping.
+            double row_delta = h == 0 ? sm.rowdelta[r] : 0.0;
+            unsigned long long row_upd = 0ull;
             for (int sw = 0; sw < cd_sweeps; sw++) {
                 bool changed = false;
                 int cur_gi = -1;
@@ -405,36 +425,51 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                     if (qc != cs[jj * CSLD + r]) {
                         // closed-form loss change, then the rank-1 gradient update (src/engine.rs:634-650)
                         const float de = __fsub_rn(cur, newdq);
-                        const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
-                        const float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
-                        my_delta = __dadd_rn(my_delta, (double)__fadd_rn(t1, t2));
+                        if (h == 0) {
+                            const float t1 = __fmul_rn(__fmul_rn(2.0f, de), gj);
+                            const float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
+                            row_delta = __dadd_rn(row_delta, (double)__fadd_rn(t1, t2));
+                        }
                         if (hss_full) {
                             const float* hrow = hss + jj * wd;
-                            for (int kk = 0; kk < wd; kk++) {
+                            for (int kk = h; kk < wd; kk += P) {
                                 float* gp = &gt[kk * LD + r];
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, hrow[kk]));
                             }
                         } else {
                             const float* hrow = H + (int64_t)j * n + c0;
-                            for (int kk = 0; kk < wd; kk++) {
+                            for (int kk = h; kk < wd; kk += P) {
                                 float* gp = &gt[kk * LD + r];
                                 *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
                             }
                         }
-                        wqs[jj * LDW + r] = newdq;
-                        cs[jj * CSLD + r] = qc;
-                        float* ep = &E[(int64_t)r * n + j];
-                        *ep = __fadd_rn(*ep, de);
-                        my_upd++;
+                        // every thread of the row has read column jj's code and W_hat before they change
+                        __syncwarp(pmask);
+                        if (h == 0) {
+                            wqs[jj * LDW + r] = newdq;
+                            cs[jj * CSLD + r] = qc;
+                            float* ep = &E[(int64_t)r * n + j];
+                            *ep = __fadd_rn(*ep, de);
+                            row_upd++;
+                        }
                         changed = true;
                     }
+                    __syncwarp(pmask);  // this column's updates are visible to the row's next decision
                 }
                 if (!changed) break;
+            }
+            if (h == 0) {
+                sm.rowdelta[r] = row_delta;
+                sm.rowupd[r] += row_upd;
             }
         }
         __syncthreads();
         unstage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         __syncthreads();
+    }
+    if (tid < BM) {
+        my_delta = sm.rowdelta[tid];
+        my_upd = sm.rowupd[tid];
     }
 }
 
