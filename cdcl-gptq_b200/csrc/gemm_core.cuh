@@ -31,6 +31,13 @@ struct Tile {
     static constexpr int BP = BN * KT / GEMM_THREADS;   // B floats fetched per thread per stage
     static constexpr int B_STAGE_FLOATS = 2 * KT * BN;  // B double buffer alone (A resident in shared memory)
     static constexpr int STAGE_FLOATS = 2 * KT * ALD + B_STAGE_FLOATS;
+    // Staged A: the row index is XOR-swizzled per k so that the QPR threads sharing a row in AGlobal::store
+    // (rows tid / QPR) write to distinct banks; the XOR keeps every aligned 4-row group contiguous.
+    static constexpr int QPR = KT / AP;
+    static constexpr int SWZ = (QPR == 2 && (4 * AP) % 32 == 0) ? 16 : (QPR == 4 && (4 * AP) % 32 == 16) ? 8 : 0;
+    static __host__ __device__ constexpr int a_swz(int k) {
+        return SWZ == 16 ? ((k / AP) & 1) * 16 : SWZ == 8 ? (((k / AP) >> 1) & 1) * 8 : 0;
+    }
     static_assert(TM == 4 || TM == 8, "BM must be 64 or 128");
     static_assert(TN == 2 || TN == 4 || TN == 8, "BN must be 32, 64 or 128");
     static_assert(AP >= 2 && BP >= 1, "stage too small");
@@ -55,12 +62,13 @@ struct TileMap {
 
 // Multiply-accumulate one KT stage held in shared memory (the first kn k-steps of it); the fragments of k-step
 // kk+1 are loaded before the products of kk are issued.
-template <class S>
+template <class S, bool SWZ>
 __device__ __forceinline__ void frag_load(float (&av)[S::TM], float (&bv)[S::TN], const float* __restrict__ As,
                                           const float* __restrict__ Bs, int kk, int ty, int tx) {
 #pragma unroll
     for (int v = 0; v < S::TM / 4; v++) {
-        float4 a = *reinterpret_cast<const float4*>(As + kk * S::ALD + ty * S::TM + 4 * v);
+        const int row = SWZ ? ((ty * S::TM + 4 * v) ^ S::a_swz(kk)) : ty * S::TM + 4 * v;
+        float4 a = *reinterpret_cast<const float4*>(As + kk * S::ALD + row);
         av[4 * v] = a.x; av[4 * v + 1] = a.y; av[4 * v + 2] = a.z; av[4 * v + 3] = a.w;
     }
     const float* brow = Bs + kk * S::BN;
@@ -76,14 +84,16 @@ __device__ __forceinline__ void frag_load(float (&av)[S::TM], float (&bv)[S::TN]
     }
 }
 
-template <class S>
+// SWZ: the A stage was written with the k-dependent row swizzle (staged operands); resident A is not swizzled.
+template <class S, bool SWZ>
 __device__ __forceinline__ void gemm_stage_mac(float (&acc)[S::TM][S::TN], const float* __restrict__ As,
                                                const float* __restrict__ Bs, int ty, int tx, int kn = S::KT) {
     float av[2][S::TM], bv[2][S::TN];
-    frag_load<S>(av[0], bv[0], As, Bs, 0, ty, tx);
+    frag_load<S, SWZ>(av[0], bv[0], As, Bs, 0, ty, tx);
 #pragma unroll
     for (int kk = 0; kk < S::KT; kk++) {
-        if (kk + 1 < S::KT && kk + 1 < kn) frag_load<S>(av[(kk + 1) & 1], bv[(kk + 1) & 1], As, Bs, kk + 1, ty, tx);
+        if (kk + 1 < S::KT && kk + 1 < kn)
+            frag_load<S, SWZ>(av[(kk + 1) & 1], bv[(kk + 1) & 1], As, Bs, kk + 1, ty, tx);
         if (kk < kn) {
 #pragma unroll
             for (int i = 0; i < S::TM; i++)
@@ -130,7 +140,7 @@ struct AGlobal {
     __device__ __forceinline__ void store(float* As, int tid, const float (&r)[S::AP]) const {
         const int row = tid / QPR, q = tid % QPR;
 #pragma unroll
-        for (int i = 0; i < S::AP; i++) As[(q * S::AP + i) * S::ALD + row] = r[i];
+        for (int i = 0; i < S::AP; i++) As[(q * S::AP + i) * S::ALD + (row ^ S::a_swz(q * S::AP + i))] = r[i];
     }
 };
 
@@ -167,7 +177,7 @@ struct AGlobalT {
     __device__ __forceinline__ void store(float* As, int tid, const float (&r)[S::AP]) const {
         const int kr = tid / TPR, c = (tid % TPR) * S::AP;
 #pragma unroll
-        for (int i = 0; i < S::AP; i++) As[kr * S::ALD + c + i] = r[i];
+        for (int i = 0; i < S::AP; i++) As[kr * S::ALD + ((c + i) ^ S::a_swz(kr))] = r[i];
     }
 };
 
@@ -238,7 +248,7 @@ __device__ void gemm_loader_a(float (&acc)[S::TM][S::TN], const AL& A, const BGl
             A.fetch(k0 + S::KT, tid, ra);
             B.fetch(k0 + S::KT, tid, rb);
         }
-        gemm_stage_mac<S>(acc, As0 + buf * S::KT * S::ALD, Bs0 + buf * S::KT * S::BN, ty, tx);
+        gemm_stage_mac<S, true>(acc, As0 + buf * S::KT * S::ALD, Bs0 + buf * S::KT * S::BN, ty, tx);
         if (more) {
             A.store(As0 + (buf ^ 1) * S::KT * S::ALD, tid, ra);
             B.store(Bs0 + (buf ^ 1) * S::KT * S::BN, tid, rb);
@@ -266,7 +276,7 @@ __device__ void gemm_smem_a(float (&acc)[S::TM][S::TN], const float* As_full, co
         const bool more = k0 + S::KT < K;
         if (more) B.fetch(k0 + S::KT, tid, rb);
         const int kn = K - k0 < S::KT ? K - k0 : S::KT;
-        gemm_stage_mac<S>(acc, As_full + (int64_t)k0 * S::ALD, Bs0 + buf * S::KT * S::BN, ty, tx, kn);
+        gemm_stage_mac<S, false>(acc, As_full + (int64_t)k0 * S::ALD, Bs0 + buf * S::KT * S::BN, ty, tx, kn);
         if (more) B.store(Bs0 + (buf ^ 1) * S::KT * S::BN, tid, rb);
         __syncthreads();
         buf ^= 1;

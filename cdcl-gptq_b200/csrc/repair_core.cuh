@@ -69,7 +69,7 @@ struct ACodes {
         const int kr = tid / TPR, c = (tid % TPR) * S::AP;
 #pragma unroll
         for (int v = 0; v < S::AP / 4; v++)
-            *reinterpret_cast<float4*>(As + kr * S::ALD + c + 4 * v) =
+            *reinterpret_cast<float4*>(As + kr * S::ALD + ((c + 4 * v) ^ S::a_swz(kr))) =
                 make_float4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
     }
 };
