@@ -40,3 +40,15 @@ def gram_accumulate(x, y, t, n, h):
     assert h.dtype == np.float64 and h.flags.c_contiguous
     check(lib().cdclq_gram_accumulate(_p(x), _p(y), t, n, _p(h)))
     return h
+
+
+def gram_accumulate_bf16_device(x_bf16, h, lower_only=False, stream=0):
+    """H (f64, device tensor, in place) += X^T X for X a (t, n) bf16 device tensor, on the tcgen05 tensor cores:
+    the token chunks of 2048 of src/linalg.rs:392 are accumulated in f32 inside the tensor core, then widened
+    into H.  With lower_only only the lower triangle of H is updated."""
+    t, n = int(x_bf16.shape[0]), int(x_bf16.shape[1])
+    assert h.shape == (n, n) and h.is_contiguous() and x_bf16.is_contiguous()
+    check(lib().cdclq_gram_accumulate_bf16_device(ctypes.c_void_p(x_bf16.data_ptr()), t, n,
+                                                  ctypes.c_void_p(h.data_ptr()), 1 if lower_only else 0,
+                                                  ctypes.c_void_p(stream)))
+    return h

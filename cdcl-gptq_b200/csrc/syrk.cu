@@ -1,12 +1,391 @@
-// syrk.cu - Hessian accumulation H += X^T X from bf16 activations on the tcgen05 tensor cores.
+// syrk.cu - Hessian accumulation H += X^T X from bf16 activations on the tcgen05 tensor cores
+// (src/linalg.rs:388-418, symmetric use x == y).
+//
+// The reference multiplies f32 activations in token chunks of 2048 (f32 products summed in f32) and widens each
+// chunk's sum into the f64 Hessian.  Here each 2048-token chunk is one f32 tensor-core accumulation in tensor
+// memory (bf16 x bf16 products are exact in f32; the summation order inside the tensor core differs from a
+// sequential sum, so this path agrees with the f32 path to f32 accumulation error, not bit for bit), then the
+// epilogue widens the chunk into the f64 Hessian in global memory, as the reference does.
+//
+// One CTA computes output tiles D[p][q] = sum_t X[t][p] X[t][q] of 128 (p) x 256 (q) channels with q >= p
+// somewhere in the tile, tiles taken round-robin by a persistent grid.  Per 64-token K block, TMA brings the
+// p block (2 boxes of 64 channels x 64 tokens) and the q block (4 boxes) into a 4-stage shared-memory ring
+// (128-byte swizzle, MN-major for the MMA: channels are contiguous in X); one thread issues four
+// 128x256x16 bf16 MMAs per block into a tensor-memory accumulator.  Two accumulators (2 x 256 columns) let the
+// four epilogue warps widen chunk c while the MMAs of chunk c+1 run.  The epilogue thread of TMEM lane p adds
+// D[p][q] into H[q][p] (lanes along a row of H: coalesced) and, unless only the lower triangle is wanted,
+// into H[p][q] for q > p, so H stays exactly symmetric.
+//
+// Roles: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31), warp 4 TMA producer, warp 5 MMA issuer and
+// TMEM owner.  Every wait on an mbarrier is bounded: on timeout the kernel records an error, leaves its loops,
+// waits (bounded) for its own copies and MMAs in flight, frees its tensor memory and returns.  No TMA multicast.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace cdclq {
 
+namespace syrk {
+
+constexpr int BMP = 128;         // tile rows p (TMEM lanes)
+constexpr int BNQ = 256;         // tile columns q
+constexpr int KB = 64;           // tokens per K block (one TMA box height)
+constexpr int CHUNK = 2048;      // tokens per f32 accumulation (src/linalg.rs:392)
+constexpr int NS = 4;            // shared-memory stages
+constexpr int BOX_BYTES = 64 * KB * 2;              // 64 channels x 64 tokens bf16 = 8 KB
+constexpr int A_BYTES = 2 * BOX_BYTES;              // 128 channels
+constexpr int B_BYTES = 4 * BOX_BYTES;              // 256 channels
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // 48 KB
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 2 * BNQ;                  // two accumulators
+constexpr size_t SMEM_BYTES = (size_t)NS * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int WAIT_LIMIT = 1 << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(smem_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the completion of the phase with the given parity; false (and the error flag set) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+    for (int it = 0; it < WAIT_LIMIT; it++) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 1023) == 1023 && *(volatile int*)err) return false;  // another role gave up
+    }
+    atomicExch(err, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of an MN-major operand with the 128-byte swizzle: 64-element (128-byte) atoms
+// along MN, `lbo` bytes apart; 8-token row groups along K, `sbo` bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;  // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: D f32, A and B bf16, both MN-major, M = 128, N = 256.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((uint32_t)(BNQ >> 3) << 17) |
+                           ((uint32_t)(BMP >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+struct Params {
+    double* h;
+    int n;
+    int64_t t;
+    int tiles_p;   // p blocks
+    int tiles_q;   // q blocks
+    int ntiles;    // tiles with q >= p somewhere
+    int lower_only;
+    int* err;
+};
+
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_q, int& pb, int& qb) {
+    // tiles of p block pb: q blocks pb/2 .. tiles_q-1 (those holding some q >= p)
+    pb = 0;
+    for (; pb < 65536; pb++) {  // tile < ntiles ends the walk within the p blocks
+        const int cnt = tiles_q - (pb >> 1);
+        if (tile < cnt) break;
+        tile -= cnt;
+    }
+    qb = (pb >> 1) + tile;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + NS * STAGE_BYTES);
+    uint64_t* empty = full + NS;
+    uint64_t* accf = empty + NS;
+    uint64_t* acce = accf + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+    __shared__ float tr[4][32 * 33];  // epilogue transposes (one 32 x 32 block per warp)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int* err = P.err;
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], 128);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+    const int n = P.n;
+    const int64_t T = P.t;
+    const int nchunks = (int)((T + CHUNK - 1) / CHUNK);
+
+    if (warp == 4) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            int ctr = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
+                int pb, qb;
+                tile_coords(tile, P.tiles_q, pb, qb);
+                const int p0 = pb * BMP, q0 = qb * BNQ;
+                for (int c = 0; c < nchunks && ok; c++) {
+                    const int64_t tok0 = (int64_t)c * CHUNK;
+                    const int nkb = (int)((min((int64_t)CHUNK, T - tok0) + KB - 1) / KB);
+                    for (int kb = 0; kb < nkb; kb++, ctr++) {
+                        const int s = ctr % NS;
+                        if (ctr >= NS && !mbar_wait(&empty[s], ((ctr / NS) - 1) & 1, err)) {
+                            ok = false;
+                            break;
+                        }
+                        unsigned char* st = base + s * STAGE_BYTES;
+                        mbar_expect_tx(&full[s], STAGE_BYTES);
+                        const int y = (int)(tok0 + (int64_t)kb * KB);
+                        tma_load_2d(st, &tmap, p0, y, &full[s]);
+                        tma_load_2d(st + BOX_BYTES, &tmap, p0 + 64, y, &full[s]);
+#pragma unroll
+                        for (int h = 0; h < 4; h++) tma_load_2d(st + A_BYTES + h * BOX_BYTES, &tmap, q0 + 64 * h, y, &full[s]);
+                    }
+                }
+            }
+            // copies still in flight land before the CTA leaves (bounded)
+            for (int k = (ctr > NS ? ctr - NS : 0); k < ctr; k++) mbar_wait(&full[k % NS], (k / NS) & 1, err);
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            int ctr = 0, acc = 0;
+            bool ok = true;
+            const uint32_t a_base = smem_u32(base);
+            for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
+                for (int c = 0; c < nchunks && ok; c++, acc++) {
+                    const int b = acc & 1;
+                    if (acc >= 2 && !mbar_wait(&acce[b], ((acc / 2) - 1) & 1, err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t d = tmem_base + (uint32_t)(b * BNQ);
+                    const int64_t tok0 = (int64_t)c * CHUNK;
+                    const int nkb = (int)((min((int64_t)CHUNK, T - tok0) + KB - 1) / KB);
+                    for (int kb = 0; kb < nkb; kb++, ctr++) {
+                        const int s = ctr % NS;
+                        if (!mbar_wait(&full[s], (ctr / NS) & 1, err)) {
+                            ok = false;
+                            mma_commit(&accf[b]);  // tracks the MMAs already issued for this chunk
+                            acc++;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t sa = a_base + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+                        for (int k = 0; k < KB / 16; k++)
+                            mma_bf16(d, smem_desc(sa + k * 2048, BOX_BYTES, 1024), smem_desc(sb + k * 2048, BOX_BYTES, 1024),
+                                     (kb | k) != 0 ? 1u : 0u);
+                        mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                    }
+                    if (!ok) break;
+                    mma_commit(&accf[b]);  // accumulator b holds chunk c
+                }
+            }
+            // every issued MMA has completed before the tensor memory is released (bounded)
+            if (acc > 0) mbar_wait(&accf[(acc - 1) & 1], ((acc - 1) / 2) & 1, err);
+        }
+    } else {
+        // ---------------- epilogue: warps 0..3, TMEM lanes 32*warp .. 32*warp+31
+        float* trw = tr[warp];
+        int acc = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
+            int pb, qb;
+            tile_coords(tile, P.tiles_q, pb, qb);
+            const int p0 = pb * BMP, q0 = qb * BNQ;
+            const int prow0 = p0 + warp * 32;  // this warp's 32 rows p
+            const int p = prow0 + lane;
+            for (int c = 0; c < nchunks; c++, acc++) {
+                const int b = acc & 1;
+                if (!mbar_wait(&accf[b], (acc / 2) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                for (int cb = 0; cb < BNQ / 32; cb++) {
+                    const int qc0 = q0 + cb * 32;
+                    float v[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BNQ + cb * 32), v);
+                    if (qc0 + 31 < prow0) continue;  // the whole 32 x 32 block has q < p
+                    // lower triangle: H[q][p] += D[p][q] (lanes along a row of H)
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const int q = qc0 + i;
+                        if (p < n && q < n && q >= p) {
+                            double* hp = P.h + (int64_t)q * n + p;
+                            *hp = __dadd_rn(*hp, (double)v[i]);
+                        }
+                    }
+                    if (!P.lower_only) {
+                        // upper triangle: H[p][q] += D[p][q] for q > p, through a transpose so lanes run along q
+#pragma unroll
+                        for (int i = 0; i < 32; i++) trw[i * 33 + lane] = v[i];
+                        __syncwarp();
+                        const int q = qc0 + lane;
+                        for (int r = 0; r < 32; r++) {
+                            const int pr = prow0 + r;
+                            if (pr < n && q < n && q > pr) {
+                                double* hp = P.h + (int64_t)pr * n + q;
+                                *hp = __dadd_rn(*hp, (double)trw[lane * 33 + r]);
+                            }
+                        }
+                        __syncwarp();
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                mbar_arrive(&acce[b]);
+            }
+        }
+    }
+
+    // teardown: every role is done with the tensor memory
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 5)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)TMEM_COLS));
+}
+
+}  // namespace syrk
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
 int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_only, cudaStream_t st) {
-    (void)x; (void)t; (void)n; (void)h; (void)lower_only; (void)st;
-    return set_error(CDCLQ_ERR_CUDA, "the bf16 tensor-core Gram kernel is not part of this build yet");
+    using namespace syrk;
+    if (t <= 0) return 0;
+    if (n % 8 != 0) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: n must be a multiple of 8 (16-byte rows)");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: x must be 16-byte aligned");
+    if (t > 0x7fffffffLL - CHUNK) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: too many tokens for one call");
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap map;
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)t};
+    cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)KB};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: tensor map encoding failed");
+    Params P;
+    P.h = h;
+    P.n = n;
+    P.t = t;
+    P.tiles_p = (n + BMP - 1) / BMP;
+    P.tiles_q = (n + BNQ - 1) / BNQ;
+    P.ntiles = 0;
+    for (int pb = 0; pb < P.tiles_p; pb++) P.ntiles += P.tiles_q - (pb >> 1);
+    P.lower_only = lower_only ? 1 : 0;
+    int* err = nullptr;
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&err, sizeof(int), st));
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    P.err = err;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = cudaFuncSetAttribute(syrk_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(err, st);
+        return cuda_error(e, "bf16 Gram smem attribute");
+    }
+    const int grid = P.ntiles < sms ? P.ntiles : sms;
+    CDCLQ_LAUNCH(syrk_bf16_kernel, grid, THREADS, SMEM_BYTES, st, map, P);
+    e = cudaGetLastError();
+    int herr = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFreeAsync(err, st);
+    if (e != cudaSuccess) return cuda_error(e, "syrk_bf16_kernel");
+    if (herr) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: a pipeline wait timed out (kernel abandoned its tiles)");
+    return 0;
 }
 
 }  // namespace cdclq

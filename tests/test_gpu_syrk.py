@@ -1,0 +1,92 @@
+"""The bf16 tensor-core Gram accumulation (cdclq_gram_accumulate_bf16_device, tcgen05) against an exact f64
+Gram of the same bf16 activations and against the bit-exact f32 path.
+
+Tolerance: the reference sums each 2048-token chunk of f32 products in f32 (src/linalg.rs:392-416); the
+tensor core sums the same exact bf16 x bf16 products in f32 in its own order.  Both differ from the exact sum
+by f32 accumulation error, bounded per chunk by 2048 * 2^-24 * sum|x_p x_q|; the tests assert every element
+within that bound of the exact Gram, and a Frobenius error no larger than the f32 path's own (x 1.5)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_tokens(torch, t, n, seed):
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    scale = torch.exp(torch.randn(n, generator=g))
+    x = (torch.randn(t, n, generator=g) * scale).to(torch.bfloat16)
+    return x
+
+
+def exact_gram(x):
+    xf = x.to(dtype=x.dtype).float().numpy().astype(np.float64)
+    return xf.T @ xf, np.abs(xf).T @ np.abs(xf)
+
+
+@pytest.mark.parametrize("t,n", [(5000, 192), (4096, 256), (2048, 136), (300, 64), (6000, 520)])
+def test_bf16_gram_matches_exact_within_f32_chunk_error(gpu, t, n):
+    import torch
+
+    from cdclq import linalg
+
+    x = bf16_tokens(torch, t, n, 1234 + n)
+    ex, ab = exact_gram(x)
+    h0 = np.random.default_rng(5).standard_normal((n, n))
+    h0 = h0 + h0.T  # a symmetric starting value: the call adds to it
+    h = torch.tensor(h0, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_bf16_device(x.cuda(), h)
+    torch.cuda.synchronize()
+    got = h.cpu().numpy() - h0
+    chunks = (t + 2047) // 2048
+    bound = chunks * 2048 * 2.0 ** -24 * ab + 1e-12
+    err = np.abs(got - ex)
+    assert np.all(err <= bound), float((err / bound).max())
+    # no less accurate than the reference's own arithmetic (sequential f32 per chunk, the bit-exact f32 path)
+    xf = x.float().numpy()
+    h_f32 = np.zeros((n, n), np.float64)
+    linalg.gram_accumulate(xf, xf, t, n, h_f32)
+    assert np.linalg.norm(got - ex) <= 1.5 * np.linalg.norm(h_f32 - ex) + 1e-9 * np.linalg.norm(ex)
+    hv = h.cpu().numpy()
+    assert np.array_equal(hv, hv.T)  # the upper triangle mirrors the lower one exactly
+
+
+def test_bf16_gram_lower_only_and_repeat(gpu):
+    import torch
+
+    from cdclq import linalg
+
+    t, n = 3000, 320
+    x = bf16_tokens(torch, t, n, 77).cuda()
+    h = torch.full((n, n), 7.0, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_bf16_device(x, h, lower_only=True)
+    linalg.gram_accumulate_bf16_device(x, h, lower_only=True)  # accumulates
+    torch.cuda.synchronize()
+    hv = h.cpu().numpy()
+    iu = np.triu_indices(n, 1)
+    assert np.all(hv[iu] == 7.0)  # upper triangle untouched
+    ex, ab = exact_gram(x.cpu())
+    il = np.tril_indices(n)
+    got = (hv - 7.0)[il]
+    bound = 2 * 2 * 2048 * 2.0 ** -24 * ab[il] + 1e-12
+    assert np.all(np.abs(got - 2 * ex[il]) <= bound)
+
+
+def test_bf16_gram_agrees_with_the_f32_path(gpu):
+    """Same activations widened to f32 through the bit-exact f32 Gram (the reference's arithmetic): both are
+    within f32 chunk-accumulation error of each other."""
+    import torch
+
+    from cdclq import linalg
+
+    t, n = 4100, 256
+    x = bf16_tokens(torch, t, n, 99)
+    h_tc = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_bf16_device(x.cuda(), h_tc)
+    torch.cuda.synchronize()
+    xf = x.float().numpy()
+    h_f32 = np.zeros((n, n), np.float64)
+    linalg.gram_accumulate(xf, xf, t, n, h_f32)
+    _, ab = exact_gram(x)
+    bound = 2 * 3 * 2048 * 2.0 ** -24 * ab + 1e-12
+    assert np.all(np.abs(h_tc.cpu().numpy() - h_f32) <= bound)
