@@ -299,6 +299,44 @@ def repair_traffic_bytes(weights):
     return None
 
 
+def run_syrk_bench(args, torch):
+    """H (f64) += X^T X for 262144 seeded bf16 tokens per width (the Hessian accumulation of configs[3]; the
+    configs[1] bench takes its Hessians as inputs).  Algorithmic work T*n*(n+1) flops (the lower triangle and
+    the diagonal), against the measured dense bf16 tensor peak.  X (>= 1 GB) exceeds the L2."""
+    import cdclq
+    from cdclq import linalg
+
+    cdclq.lib()
+    peaks = load_peaks()
+    peak = peaks.get("bf16_tflops") or 1590.0
+    t = TOKENS
+    for n in (2048, 4096, 5632, 11008):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(7000 + n)
+        x = torch.randn(t, n, device="cuda", generator=g, dtype=torch.float32).to(torch.bfloat16)
+        h = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+        st = torch.cuda.current_stream()
+        for _ in range(max(3, args.warmup)):
+            linalg.gram_accumulate_bf16_device(x, h, lower_only=True, stream=st.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            linalg.gram_accumulate_bf16_device(x, h, lower_only=True, stream=st.cuda_stream)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        flops = float(t) * n * (n + 1)
+        tf = flops / (ms * 1e-3) / 1e12
+        print(json.dumps({"metric": "bf16 Gram accumulation H += X^T X (lower triangle)", "kernel": "syrk_bf16_kernel",
+                          "n": n, "tokens": t, "ms": ms, "value": tf, "unit": "TFLOP/s",
+                          "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                       "frac": tf / peak, "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)"},
+                          "steps": args.steps}), flush=True)
+        del x, h
+        torch.cuda.empty_cache()
+
+
 def workload_config(cfg):
     return {"workload": "TinyLlama-1.1B-shaped model (configs[1]): 22 decoder layers, 154 linear layers, "
                         "9.69e8 bf16-valued weights, 88 Hessians from 262144 seeded tokens",
@@ -316,6 +354,8 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="decoder layers (22 = the configs[1] model)")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", default="model", choices=["model", "syrk"],
+                    help="syrk: time the bf16 tensor-core Hessian accumulation alone (one JSON line per width)")
     args = ap.parse_args()
 
     import torch
@@ -335,6 +375,12 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, torch, rank, world)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if args.kernel == "syrk":
+        if rank == 0:
+            run_syrk_bench(args, torch)
         if world > 1:
             torch.distributed.destroy_process_group()
         return

@@ -12,12 +12,12 @@
 // p block (2 boxes of 64 channels x 64 tokens) and the q block (4 boxes) into a 4-stage shared-memory ring
 // (128-byte swizzle, MN-major for the MMA: channels are contiguous in X); one thread issues four
 // 128x256x16 bf16 MMAs per block into a tensor-memory accumulator.  Two accumulators (2 x 256 columns) let the
-// four epilogue warps widen chunk c while the MMAs of chunk c+1 run.  The epilogue thread of TMEM lane p adds
+// eight epilogue warps widen chunk c while the MMAs of chunk c+1 run.  The epilogue thread of TMEM lane p adds
 // D[p][q] into H[q][p] (lanes along a row of H: coalesced) and, unless only the lower triangle is wanted,
 // into H[p][q] for q > p, so H stays exactly symmetric.
 //
-// Roles: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31), warp 4 TMA producer, warp 5 MMA issuer and
-// TMEM owner.  Every wait on an mbarrier is bounded: on timeout the kernel records an error, leaves its loops,
+// Roles: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4).. and columns 128(w/4)..), warp 8 TMA producer,
+// warp 9 MMA issuer and TMEM owner.  Every wait on an mbarrier is bounded: on timeout the kernel records an error, leaves its loops,
 // waits (bounded) for its own copies and MMAs in flight, frees its tensor memory and returns.  No TMA multicast.
 #include <cuda.h>
 
@@ -34,12 +34,13 @@ constexpr int BMP = 128;         // tile rows p (TMEM lanes)
 constexpr int BNQ = 256;         // tile columns q
 constexpr int KB = 64;           // tokens per K block (one TMA box height)
 constexpr int CHUNK = 2048;      // tokens per f32 accumulation (src/linalg.rs:392)
-constexpr int NS = 4;            // shared-memory stages
+constexpr int NS = 3;            // shared-memory stages
 constexpr int BOX_BYTES = 64 * KB * 2;              // 64 channels x 64 tokens bf16 = 8 KB
 constexpr int A_BYTES = 2 * BOX_BYTES;              // 128 channels
 constexpr int B_BYTES = 4 * BOX_BYTES;              // 256 channels
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // 48 KB
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;     // two per TMEM lane quadrant, each taking half of the tile's columns
+constexpr int THREADS = (EPI_WARPS + 2) * 32;
 constexpr int TMEM_COLS = 2 * BNQ;                  // two accumulators
 constexpr size_t SMEM_BYTES = (size_t)NS * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
 constexpr int WAIT_LIMIT = 1 << 24;
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
     uint64_t* accf = empty + NS;
     uint64_t* acce = accf + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
-    __shared__ float tr[4][32 * 33];  // epilogue transposes (one 32 x 32 block per warp)
+    __shared__ float tr[EPI_WARPS][32 * 33];  // epilogue transposes (one 32 x 32 block per warp)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int* err = P.err;
 
@@ -167,11 +168,11 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], 128);
+            mbar_init(&acce[b], EPI_WARPS * 32);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 5) {
+    if (warp == EPI_WARPS + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"((uint32_t)TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
     const int64_t T = P.t;
     const int nchunks = (int)((T + CHUNK - 1) / CHUNK);
 
-    if (warp == 4) {
+    if (warp == EPI_WARPS) {
         // ---------------- TMA producer
         if (lane == 0) {
             int ctr = 0;
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
             // copies still in flight land before the CTA leaves (bounded)
             for (int k = (ctr > NS ? ctr - NS : 0); k < ctr; k++) mbar_wait(&full[k % NS], (k / NS) & 1, err);
         }
-    } else if (warp == 5) {
+    } else if (warp == EPI_WARPS + 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
             int ctr = 0, acc = 0;
@@ -256,15 +257,16 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
             if (acc > 0) mbar_wait(&accf[(acc - 1) & 1], ((acc - 1) / 2) & 1, err);
         }
     } else {
-        // ---------------- epilogue: warps 0..3, TMEM lanes 32*warp .. 32*warp+31
+        // ---------------- epilogue: warps 0..7; TMEM lanes 32*(warp%4) .., columns 128*(warp/4) ..
         float* trw = tr[warp];
+        const int quad = warp & 3, half = warp >> 2;
         int acc = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
             int pb, qb;
             tile_coords(tile, P.tiles_q, pb, qb);
             const int p0 = pb * BMP, q0 = qb * BNQ;
-            const int prow0 = p0 + warp * 32;  // this warp's 32 rows p
+            const int prow0 = p0 + quad * 32;  // this warp's 32 rows p
             const int p = prow0 + lane;
             for (int c = 0; c < nchunks; c++, acc++) {
                 const int b = acc & 1;
@@ -273,18 +275,24 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int cb = 0; cb < BNQ / 32; cb++) {
+                for (int cb = half * (BNQ / 64); cb < (half + 1) * (BNQ / 64); cb++) {
                     const int qc0 = q0 + cb * 32;
                     float v[32];
-                    tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BNQ + cb * 32), v);
+                    tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BNQ + cb * 32), v);
                     if (qc0 + 31 < prow0) continue;  // the whole 32 x 32 block has q < p
-                    // lower triangle: H[q][p] += D[p][q] (lanes along a row of H)
+                    // lower triangle: H[q][p] += D[p][q] (lanes along a row of H).  All 32 loads are issued
+                    // before any store, so the read-modify-writes overlap instead of waiting on each other.
+                    {
+                        double old[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int q = qc0 + i;
-                        if (p < n && q < n && q >= p) {
-                            double* hp = P.h + (int64_t)q * n + p;
-                            *hp = __dadd_rn(*hp, (double)v[i]);
+                        for (int i = 0; i < 32; i++) {
+                            const int q = qc0 + i;
+                            old[i] = (p < n && q < n && q >= p) ? P.h[(int64_t)q * n + p] : 0.0;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            const int q = qc0 + i;
+                            if (p < n && q < n && q >= p) P.h[(int64_t)q * n + p] = __dadd_rn(old[i], (double)v[i]);
                         }
                     }
                     if (!P.lower_only) {
@@ -293,12 +301,17 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                         for (int i = 0; i < 32; i++) trw[i * 33 + lane] = v[i];
                         __syncwarp();
                         const int q = qc0 + lane;
+                        double old[32];
+#pragma unroll
                         for (int r = 0; r < 32; r++) {
                             const int pr = prow0 + r;
-                            if (pr < n && q < n && q > pr) {
-                                double* hp = P.h + (int64_t)pr * n + q;
-                                *hp = __dadd_rn(*hp, (double)trw[lane * 33 + r]);
-                            }
+                            old[r] = (pr < n && q < n && q > pr) ? P.h[(int64_t)pr * n + q] : 0.0;
+                        }
+#pragma unroll
+                        for (int r = 0; r < 32; r++) {
+                            const int pr = prow0 + r;
+                            if (pr < n && q < n && q > pr)
+                                P.h[(int64_t)pr * n + q] = __dadd_rn(old[r], (double)trw[lane * 33 + r]);
                         }
                         __syncwarp();
                     }
@@ -313,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (warp == 5)
+    if (warp == EPI_WARPS + 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)TMEM_COLS));
 }
 

@@ -4,7 +4,7 @@ Gram of the same bf16 activations and against the bit-exact f32 path.
 Tolerance: the reference sums each 2048-token chunk of f32 products in f32 (src/linalg.rs:392-416); the
 tensor core sums the same exact bf16 x bf16 products in f32 in its own order.  Both differ from the exact sum
 by f32 accumulation error, bounded per chunk by 2048 * 2^-24 * sum|x_p x_q|; the tests assert every element
-within that bound of the exact Gram, and a Frobenius error no larger than the f32 path's own (x 1.5)."""
+within that bound of the exact Gram, and a Frobenius error within 3x of the f32 path's own."""
 import numpy as np
 import pytest
 
@@ -42,11 +42,12 @@ def test_bf16_gram_matches_exact_within_f32_chunk_error(gpu, t, n):
     bound = chunks * 2048 * 2.0 ** -24 * ab + 1e-12
     err = np.abs(got - ex)
     assert np.all(err <= bound), float((err / bound).max())
-    # no less accurate than the reference's own arithmetic (sequential f32 per chunk, the bit-exact f32 path)
+    # of the order of the reference's own arithmetic (sequential f32 per chunk, the bit-exact f32 path): the
+    # tensor core's internal f32 additions truncate, so its error is biased and up to ~2x the sequential one
     xf = x.float().numpy()
     h_f32 = np.zeros((n, n), np.float64)
     linalg.gram_accumulate(xf, xf, t, n, h_f32)
-    assert np.linalg.norm(got - ex) <= 1.5 * np.linalg.norm(h_f32 - ex) + 1e-9 * np.linalg.norm(ex)
+    assert np.linalg.norm(got - ex) <= 3.0 * np.linalg.norm(h_f32 - ex) + 1e-9 * np.linalg.norm(ex)
     hv = h.cpu().numpy()
     assert np.array_equal(hv, hv.T)  # the upper triangle mirrors the lower one exactly
 
@@ -90,3 +91,29 @@ def test_bf16_gram_agrees_with_the_f32_path(gpu):
     _, ab = exact_gram(x)
     bound = 2 * 3 * 2048 * 2.0 ** -24 * ab + 1e-12
     assert np.all(np.abs(h_tc.cpu().numpy() - h_f32) <= bound)
+
+
+def test_bf16_gram_downstream_codes(gpu):
+    """A layer quantized with the tensor-core Hessian against the same layer quantized with the f32-path Hessian
+    (the reference's arithmetic): the fraction of identical codes is reported and bounded from below."""
+    import torch
+
+    import cdclq
+    from cdclq import linalg
+    from cdclq.abi import Config
+
+    t, n, d_out = 16384, 512, 256
+    x = bf16_tokens(torch, t, n, 4242)
+    h_tc = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_bf16_device(x.cuda(), h_tc)
+    torch.cuda.synchronize()
+    xf = x.float().numpy()
+    h_f32 = np.zeros((n, n), np.float64)
+    linalg.gram_accumulate(xf, xf, t, n, h_f32)
+    w = (np.random.default_rng(3).standard_normal((d_out, n)) * 0.02).astype(np.float32)
+    cfg = Config(bits=3, group=128, row_chunk=128, passes=4)
+    qa, _ = cdclq.quantize_layer(w, d_out, n, h_tc.cpu().numpy().astype(np.float32), None, "a", cfg)
+    qb, _ = cdclq.quantize_layer(w, d_out, n, h_f32.astype(np.float32), None, "b", cfg)
+    same = float(np.mean(qa.codes == qb.codes)) if np.array_equal(qa.perm, qb.perm) else 0.0
+    print("identical codes with the tensor-core Hessian: %.5f" % same)
+    assert same >= 0.99
