@@ -29,7 +29,7 @@ static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~
 size_t phase1_smem_bytes(int block) {
     size_t b = (size_t)block;
     return align16(b * P1_W1LD * 4) + align16(b * P1_ELD * 4) + align16(b * P1_ROWS) +
-           (size_t)P1Tile::B_STAGE_FLOATS * 4;
+           (size_t)P1Tile::B_STAGE_FLOATS * 4 + align16(b * 4);
 }
 
 __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __restrict__ items, int B, int mse) {
@@ -44,6 +44,7 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
     float* err1 = reinterpret_cast<float*>(smem_raw + align16((size_t)B * P1_W1LD * 4));
     uint8_t* cbuf = smem_raw + align16((size_t)B * P1_W1LD * 4) + align16((size_t)B * P1_ELD * 4);
     float* stage = reinterpret_cast<float*>(cbuf + align16((size_t)B * P1_ROWS));
+    float* invd = stage + P1Tile::B_STAGE_FLOATS;  // [B] 1 / U_jj of the block's columns
 
     float* w = it.w + (int64_t)it.row0 * n;  // tile rows: w[rr * n + c]
     const float* U = it.u;
@@ -56,6 +57,7 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
             w1[k * P1_W1LD + rr] = (rr < rows) ? w[(int64_t)rr * n + i1 + k] : 0.0f;
         }
         for (int idx = tid; idx < P1_ELD * cnt; idx += blockDim.x) err1[idx] = 0.0f;
+        for (int k = tid; k < cnt; k += blockDim.x) invd[k] = __fdiv_rn(1.0f, __ldg(U + (int64_t)(i1 + k) * n + i1 + k));
         __syncthreads();
 
         for (int i = 0; i < cnt; i++) {
@@ -82,24 +84,35 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
                 }
                 grid_mk(xmin, xmax, maxq, s, z);
                 if (mse) {
-                    float best_err = INFINITY;
-                    int best_i = 24;
-                    for (int ci = sub; ci < 24; ci += 4) {
-                        float p = clip_ratio(ci), cs, cz;
-                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, cs, cz);
-                        float err = 0.0f;
-                        for (int col = j; col < gend; col++) {
-                            float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r]
-                                                 : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+                    // this thread's 6 of the 24 clip candidates (ci = sub + 4m), each error summed over the
+                    // group's columns in order; one read of each value feeds all six
+                    constexpr int NC = 24 / 4;
+                    float cs[NC], cz[NC], cerr[NC];
+#pragma unroll
+                    for (int m = 0; m < NC; m++) {
+                        const float p = clip_ratio(sub + 4 * m);
+                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, cs[m], cz[m]);
+                        cerr[m] = 0.0f;
+                    }
+                    for (int col = j; col < gend; col++) {
+                        const float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r]
+                                                   : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+#pragma unroll
+                        for (int m = 0; m < NC; m++) {
                             uint8_t c;
                             float d;
-                            quant_code(v, cs, cz, maxq, c, d);
-                            float e = __fsub_rn(d, v);
-                            err = __fadd_rn(err, __fmul_rn(e, e));
+                            quant_code(v, cs[m], cz[m], maxq, c, d);
+                            const float e = __fsub_rn(d, v);
+                            cerr[m] = __fadd_rn(cerr[m], __fmul_rn(e, e));
                         }
-                        if (err < best_err) {
-                            best_err = err;
-                            best_i = ci;
+                    }
+                    float best_err = INFINITY;
+                    int best_i = 24;
+#pragma unroll
+                    for (int m = 0; m < NC; m++) {
+                        if (cerr[m] < best_err) {
+                            best_err = cerr[m];
+                            best_i = sub + 4 * m;
                         }
                     }
                     // first index of the strict minimum == min error, ties to the smaller index
@@ -128,7 +141,7 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
             uint8_t c;
             float dq;
             quant_code(wv, s, z, maxq, c, dq);
-            const float inv_d = __fdiv_rn(1.0f, __ldg(U + (int64_t)j * n + j));
+            const float inv_d = invd[i];
             const float e = __fmul_rn(__fsub_rn(wv, dq), inv_d);
             __syncwarp();
             if (sub == 0) {
