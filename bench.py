@@ -309,8 +309,8 @@ def run_syrk_bench(args, torch):
     cdclq.lib()
     peaks = load_peaks()
     peak = peaks.get("bf16_tflops") or 1590.0
-    t = TOKENS
-    for n in (2048, 4096, 5632, 11008):
+    t = args.syrk_tokens
+    for n in [int(v) for v in args.syrk_widths.split(",")]:
         g = torch.Generator(device="cuda")
         g.manual_seed(7000 + n)
         x = torch.randn(t, n, device="cuda", generator=g, dtype=torch.float32).to(torch.bfloat16)
@@ -356,6 +356,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", default="model", choices=["model", "syrk"],
                     help="syrk: time the bf16 tensor-core Hessian accumulation alone (one JSON line per width)")
+    ap.add_argument("--syrk-widths", default="2048,4096,5632,11008", help="--kernel syrk: channel counts n")
+    ap.add_argument("--syrk-tokens", type=int, default=TOKENS, help="--kernel syrk: tokens per Hessian")
     args = ap.parse_args()
 
     import torch

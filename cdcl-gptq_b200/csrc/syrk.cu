@@ -134,8 +134,19 @@ struct Params {
     int tiles_q;   // q blocks
     int ntiles;    // tiles with q >= p somewhere
     int lower_only;
+    int nseg;        // token segments per tile (split over CTAs when there are few tiles)
+    int cps;         // chunks per segment
+    double* scratch; // nseg > 1: per (segment, tile) f64 partial sums, [q][p] within a tile
     int* err;
 };
+
+// Work item -> (tile, chunk range); items are segment-major so that the CTAs of a wave read the same tokens.
+__device__ __forceinline__ void item_range(const Params& P, int item, int nchunks, int& tile, int& c0, int& c1) {
+    const int seg = item / P.ntiles;
+    tile = item - seg * P.ntiles;
+    c0 = seg * P.cps;
+    c1 = min(nchunks, c0 + P.cps);
+}
 
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_q, int& pb, int& qb) {
@@ -190,11 +201,12 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
         if (lane == 0) {
             int ctr = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
-                int pb, qb;
+            for (int item = blockIdx.x; item < P.ntiles * P.nseg && ok; item += gridDim.x) {
+                int tile, c0, c1, pb, qb;
+                item_range(P, item, nchunks, tile, c0, c1);
                 tile_coords(tile, P.tiles_q, pb, qb);
                 const int p0 = pb * BMP, q0 = qb * BNQ;
-                for (int c = 0; c < nchunks && ok; c++) {
+                for (int c = c0; c < c1 && ok; c++) {
                     const int64_t tok0 = (int64_t)c * CHUNK;
                     const int nkb = (int)((min((int64_t)CHUNK, T - tok0) + KB - 1) / KB);
                     for (int kb = 0; kb < nkb; kb++, ctr++) {
@@ -222,8 +234,10 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
             int ctr = 0, acc = 0;
             bool ok = true;
             const uint32_t a_base = smem_u32(base);
-            for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
-                for (int c = 0; c < nchunks && ok; c++, acc++) {
+            for (int item = blockIdx.x; item < P.ntiles * P.nseg && ok; item += gridDim.x) {
+                int tile, c0, c1;
+                item_range(P, item, nchunks, tile, c0, c1);
+                for (int c = c0; c < c1 && ok; c++, acc++) {
                     const int b = acc & 1;
                     if (acc >= 2 && !mbar_wait(&acce[b], ((acc / 2) - 1) & 1, err)) {
                         ok = false;
@@ -262,13 +276,15 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
         const int quad = warp & 3, half = warp >> 2;
         int acc = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
-            int pb, qb;
+        for (int item = blockIdx.x; item < P.ntiles * P.nseg && ok; item += gridDim.x) {
+            int tile, c0, c1, pb, qb;
+            item_range(P, item, nchunks, tile, c0, c1);
             tile_coords(tile, P.tiles_q, pb, qb);
             const int p0 = pb * BMP, q0 = qb * BNQ;
             const int prow0 = p0 + quad * 32;  // this warp's 32 rows p
             const int p = prow0 + lane;
-            for (int c = 0; c < nchunks; c++, acc++) {
+            double* part = P.scratch + (int64_t)item * (BMP * BNQ);  // nseg > 1
+            for (int c = c0; c < c1; c++, acc++) {
                 const int b = acc & 1;
                 if (!mbar_wait(&accf[b], (acc / 2) & 1, err)) {
                     ok = false;
@@ -280,6 +296,21 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                     float v[32];
                     tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BNQ + cb * 32), v);
                     if (qc0 + 31 < prow0) continue;  // the whole 32 x 32 block has q < p
+                    if (P.nseg > 1) {
+                        // this segment's partial: (double) of its first chunk, then sequential f64 adds
+                        double* dst = part + (int64_t)(qc0 - q0) * BMP + (p - p0);
+                        if (c == c0) {
+#pragma unroll
+                            for (int i = 0; i < 32; i++) dst[i * BMP] = (double)v[i];
+                        } else {
+                            double old[32];
+#pragma unroll
+                            for (int i = 0; i < 32; i++) old[i] = dst[i * BMP];
+#pragma unroll
+                            for (int i = 0; i < 32; i++) dst[i * BMP] = __dadd_rn(old[i], (double)v[i]);
+                        }
+                        continue;
+                    }
                     // lower triangle: H[q][p] += D[p][q] (lanes along a row of H).  All 32 loads are issued
                     // before any store, so the read-modify-writes overlap instead of waiting on each other.
                     {
@@ -332,6 +363,33 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
 
 }  // namespace syrk
 
+namespace syrk {
+
+// Split tiles: H[q][p] += partial_0 + partial_1 + ... (segments in order), and the mirror for q > p.
+// Block = 128 threads (p within the tile), grid = (tiles, 256 / 32 column groups).
+__global__ void __launch_bounds__(128) syrk_reduce_kernel(const Params P) {
+    const int tile = blockIdx.x;
+    int pb, qb;
+    tile_coords(tile, P.tiles_q, pb, qb);
+    const int pl = threadIdx.x, p = pb * BMP + pl, n = P.n;
+    if (p >= n) return;
+    for (int ql = blockIdx.y * 32; ql < blockIdx.y * 32 + 32; ql++) {
+        const int q = qb * BNQ + ql;
+        if (q >= n || q < p) continue;
+        double lo = P.h[(int64_t)q * n + p];
+        double up = (!P.lower_only && q > p) ? P.h[(int64_t)p * n + q] : 0.0;
+        for (int sg = 0; sg < P.nseg; sg++) {
+            const double v = P.scratch[((int64_t)sg * P.ntiles + tile) * (BMP * BNQ) + (int64_t)ql * BMP + pl];
+            lo = __dadd_rn(lo, v);
+            up = __dadd_rn(up, v);
+        }
+        P.h[(int64_t)q * n + p] = lo;
+        if (!P.lower_only && q > p) P.h[(int64_t)p * n + q] = up;
+    }
+}
+
+}  // namespace syrk
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -377,25 +435,45 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     P.ntiles = 0;
     for (int pb = 0; pb < P.tiles_p; pb++) P.ntiles += P.tiles_q - (pb >> 1);
     P.lower_only = lower_only ? 1 : 0;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // fewer tiles than SMs (small n): split each tile's tokens into segments so that every SM gets about four
+    // items; with a wave or more of tiles the per-segment partials cost more than the idle tail saves
+    const int nchunks = (int)((t + CHUNK - 1) / CHUNK);
+    int nseg = P.ntiles >= sms ? 1 : (4 * sms + P.ntiles - 1) / P.ntiles;
+    if (nseg > nchunks) nseg = nchunks;
+    if (nseg < 1) nseg = 1;
+    P.cps = (nchunks + nseg - 1) / nseg;
+    P.nseg = (nchunks + P.cps - 1) / P.cps;
+    P.scratch = nullptr;
+    if (P.nseg > 1)
+        CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&P.scratch,
+                                       sizeof(double) * (size_t)P.nseg * P.ntiles * BMP * BNQ, st));
     int* err = nullptr;
     CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&err, sizeof(int), st));
     CDCLQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     P.err = err;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaError_t e = cudaFuncSetAttribute(syrk_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) {
         cudaFreeAsync(err, st);
+        if (P.scratch) cudaFreeAsync(P.scratch, st);
         return cuda_error(e, "bf16 Gram smem attribute");
     }
-    const int grid = P.ntiles < sms ? P.ntiles : sms;
+    const int items = P.ntiles * P.nseg;
+    const int grid = items < sms ? items : sms;
     CDCLQ_LAUNCH(syrk_bf16_kernel, grid, THREADS, SMEM_BYTES, st, map, P);
     e = cudaGetLastError();
+    if (e == cudaSuccess && P.nseg > 1) {
+        dim3 rg(P.ntiles, BNQ / 32);
+        CDCLQ_LAUNCH(syrk_reduce_kernel, rg, BMP, 0, st, P);
+        e = cudaGetLastError();
+    }
     int herr = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFreeAsync(err, st);
+    if (P.scratch) cudaFreeAsync(P.scratch, st);
     if (e != cudaSuccess) return cuda_error(e, "syrk_bf16_kernel");
     if (herr) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: a pipeline wait timed out (kernel abandoned its tiles)");
     return 0;
