@@ -499,6 +499,33 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     std::vector<size_t> w_uploads;  // host weights copied behind the Hessians
     std::vector<std::vector<uint32_t>> input_perm(nin);  // cache of the W-independent permutation
     std::vector<char> input_perm_done(nin, 0);
+    {
+        // The W-independent permutations of all inputs (act-order sorts of n keys each) on host threads.
+        std::vector<size_t> todo;
+        for (const auto& L : layers) {
+            const size_t n = inputs[L.input].n, g = effective_group(cfg, n);
+            const bool skel = cfg.skeleton_pct > 0.0 && g < n;
+            if (!skel && !input_perm_done[L.input]) {
+                input_perm_done[L.input] = 1;
+                todo.push_back(L.input);
+            }
+        }
+        if (!todo.empty()) {
+            CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));  // the diagonals are on the host
+            const size_t nt = std::max<size_t>(1, std::min(todo.size(), host_threads()));
+            auto work = [&](size_t t0) {
+                for (size_t k = t0; k < todo.size(); k += nt) {
+                    const size_t in = todo[k], n = inputs[in].n;
+                    size_t ns = 0;
+                    compute_perm(hdiag[in], nullptr, n, effective_group(cfg, n), cfg, input_perm[in], ns);
+                }
+            };
+            std::vector<std::thread> pool;
+            for (size_t t = 1; t < nt; t++) pool.emplace_back(work, t);
+            work(0);
+            for (auto& th : pool) th.join();
+        }
+    }
     for (size_t li = 0; li < layers.size(); li++) {
         const LayerReq& L = layers[li];
         LayerPlan& P = plans[li];
@@ -528,12 +555,6 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             compute_perm(hdiag[L.input], &colsq, P.n, P.g, cfg, P.perm, P.nskel);
             ar.free_one(cs_dev);
         } else {
-            if (!input_perm_done[L.input]) {
-                CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
-                size_t ns = 0;
-                compute_perm(hdiag[L.input], nullptr, P.n, P.g, cfg, input_perm[L.input], ns);
-                input_perm_done[L.input] = 1;
-            }
             P.perm = input_perm[L.input];
             P.nskel = 0;
         }
