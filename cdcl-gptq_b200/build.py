@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "cdclq", "libcdclq_cuda.so")
 SOURCES = ["engine.cu", "prep.cu", "gptq.cu", "repair.cu", "repair_bm64.cu", "repair_bm128.cu", "gemm.cu", "pack.cu",
-           "syrk.cu", "noalloc.cu"]
+           "syrk.cu", "noalloc.cu", "io.cu"]
 HEADERS = ["common.cuh", "gemm_core.cuh", "kernels.h", "repair_core.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC"]

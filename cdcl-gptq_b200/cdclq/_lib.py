@@ -33,6 +33,11 @@ SIGNATURES = {
                                       ctypes.POINTER(CLayerStats), P]),
     "cdclq_row_chunk": (SZ, [CFG, SZ]),
     "cdclq_quantize_batch": (I32, [ctypes.POINTER(CBatchInput), SZ, ctypes.POINTER(CBatchLayer), SZ, CFG, I32, P]),
+    "cdclq_widen_to_f32_device": (I32, [P, I32, SZ, P, P]),
+    "cdclq_first_non_finite_device": (I32, [P, SZ, P, P]),
+    "cdclq_check_matrix_device": (I32, [P, SZ, ctypes.c_char_p, P]),
+    "cdclq_pack_device": (I32, [P, SZ, SZ, SZ, P, P, P]),
+    "cdclq_encode_groups_device": (I32, [P, P, SZ, P, P, P]),
     "cdclq_prepare_factors": (I32, [ctypes.POINTER(CBatchInput), SZ, P, SZ, CFG, P, I32, P]),
     "cdclq_quantize_batch_prepared": (I32, [ctypes.POINTER(CBatchInput), SZ, P, ctypes.POINTER(CBatchLayer), SZ, CFG,
                                             I32, P]),

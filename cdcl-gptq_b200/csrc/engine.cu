@@ -1499,6 +1499,24 @@ int cdclq_pack(const uint8_t* codes, size_t d_out, size_t n, size_t g, const uin
     return CDCLQ_OK;
 }
 
+int cdclq_pack_device(const uint8_t* codes, size_t d_out, size_t n, size_t g, const uint8_t* gbits, uint8_t* out,
+                      void* stream) {
+    if (!codes || !gbits || !out || g == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
+    cudaStream_t st = (cudaStream_t)stream;
+    Arena ar(st);
+    size_t ng = (n + g - 1) / g, rb = cdclq_row_bytes(n, g, gbits);
+    std::vector<uint32_t> off = bit_offsets(n, g, gbits);
+    uint8_t* gd = nullptr;
+    uint32_t* offd = nullptr;
+    int rc = 0;
+    if ((rc = ar.alloc(&gd, ng)) || (rc = ar.alloc(&offd, n + 1))) return rc;
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(gd, gbits, ng, cudaMemcpyHostToDevice, st));
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(offd, off.data(), (n + 1) * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+    if ((rc = launch_pack(codes, (int)d_out, (int)n, (int)g, gd, offd, (int)rb, out, st))) return rc;
+    CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));  // the staged offsets outlive the kernel
+    return CDCLQ_OK;
+}
+
 int cdclq_unpack_dequant(const uint8_t* packed, size_t d_out, size_t n, size_t g, const uint8_t* gbits,
                          const uint32_t* perm, const float* scales, const float* zeros, float* out) {
     if (!packed || !gbits || !perm || !scales || !zeros || !out || g == 0)

@@ -153,6 +153,27 @@ typedef struct cdclq_batch_layer {
 int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
                          size_t n_layers, const cdclq_config* cfg, int on_device, void* stream);
 
+/* ---- ingest and packed output on the device (src/io.rs) ------------------------------------------------- */
+
+#define CDCLQ_DTYPE_F32 0
+#define CDCLQ_DTYPE_F16 1
+#define CDCLQ_DTYPE_BF16 2
+/* tensor_to_f32 (src/io.rs:37-45) on the device: dst[i] = (f32) src[i] for a tensor copied raw from a safetensors
+ * file (dtype CDCLQ_DTYPE_*); the widening is lossless.  Device pointers. */
+int cdclq_widen_to_f32_device(const void* src, int dtype, size_t count, float* dst, void* stream);
+/* first_non_finite (src/io.rs:120-122) on the device: index of the first NaN/inf of x (device), -1 if none. */
+int cdclq_first_non_finite_device(const float* x, size_t count, int64_t* index_out, void* stream);
+/* The load-time check of HessianStore::tensor (src/io.rs:204-211): CDCLQ_ERR_NONFINITE with the reference's
+ * message ("<key>: <n> x <n> matrix has a non-finite entry (<v>) at [ <r>, <c> ]; ...") when the device matrix
+ * h (n x n) holds a NaN or an infinity. */
+int cdclq_check_matrix_device(const float* h, size_t n, const char* key, void* stream);
+/* QLayer::pack (src/quant.rs:113-151) with device codes and output (out: d_out x row_bytes). gbits is host. */
+int cdclq_pack_device(const uint8_t* codes, size_t d_out, size_t n, size_t g, const uint8_t* gbits, uint8_t* out,
+                      void* stream);
+/* The group encodings of packed_tensors (src/io.rs:248-251): scales as f16 bits, zero points as u8 (device). */
+int cdclq_encode_groups_device(const float* scales, const float* zeros, size_t count, uint16_t* scales_f16,
+                               uint8_t* qzeros, void* stream);
+
 /* ---- multi-GPU: factorisations spread over ranks (the "compute once on the owning GPU, then broadcast"
  * option for Prepared's U, src/engine.rs:320-342; the reference itself runs on one host) ----------------- */
 
