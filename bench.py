@@ -242,7 +242,7 @@ def cpu_sample(layers, inputs, H, W, cfg):
         chunks = (d_out + ROW_CHUNK - 1) // ROW_CHUNK
         per_block += t_chunk[d_in] * chunks / cores
     model_s = N_LAYERS * per_block
-    weights = sum(l[1] * l[2] for l in layers)
+    weights = N_LAYERS * sum(d_out * d_in for (_, d_out, d_in, _) in BLOCK)  # the whole model, as model_s
     return {
         "value": weights / model_s, "unit": "weights/s", "cores": cores, "kind": "port",
         "seconds_per_model": model_s, "sample_wall_s": wall,
