@@ -8,7 +8,8 @@ algorithm:
 
   * rows: every layer's rows are split in whole row chunks, a contiguous range per rank (rows are
     independent, src/engine.rs:9-15; conflict selection and the tol stop are per row chunk,
-    src/engine.rs:480-511, 660-665, so chunk boundaries must not move);
+    src/engine.rs:480-511, 660-665, so chunk boundaries must not move); the assignment of ranges to ranks
+    rotates from layer to layer, so that leftover chunks spread over the ranks;
   * factorisations: the distinct inputs are assigned to ranks by longest-processing-time on n^3 (Cholesky +
     triangular inverse), each rank factorises its share (cdclq_prepare_factors) and every factor U is then
     broadcast from its owner, so no rank repeats another's factorisation;
@@ -25,11 +26,13 @@ from ._lib import check, lib
 from .abi import CBatchInput, CBatchLayer, CLayerStats, num_groups
 
 
-def shard_rows(d_out, row_chunk, rank, world):
-    """Contiguous row range [r0, r1) of `rank`, in whole row chunks of `row_chunk` rows."""
+def shard_rows(d_out, row_chunk, rank, world, rotate=0):
+    """Contiguous row range [r0, r1) of `rank`, in whole row chunks of `row_chunk` rows.  `rotate` shifts which
+    rank takes which range, so that the layers of a model hand their leftover chunks to different ranks."""
     chunks = (d_out + row_chunk - 1) // row_chunk
-    c0 = chunks * rank // world
-    c1 = chunks * (rank + 1) // world
+    v = (rank + rotate) % world
+    c0 = chunks * v // world
+    c1 = chunks * (v + 1) // world
     return min(c0 * row_chunk, d_out), min(c1 * row_chunk, d_out)
 
 
@@ -78,8 +81,8 @@ class ModelBatch:
         if rc <= 0 and world > 1:
             raise ValueError("multi-GPU row sharding needs a pinned row_chunk (row chunks must not move)")
         rows = []
-        for (name, d_out, d_in, inp), w in zip(layers, W):
-            r0, r1 = shard_rows(d_out, rc, rank, world) if world > 1 else (0, d_out)
+        for li, ((name, d_out, d_in, inp), w) in enumerate(zip(layers, W)):
+            r0, r1 = shard_rows(d_out, rc, rank, world, rotate=li) if world > 1 else (0, d_out)
             if r1 > r0:
                 rows.append((name, d_out, d_in, inp, w, r0, r1))
         self.names = [r[0] for r in rows]

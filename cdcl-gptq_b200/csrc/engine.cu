@@ -902,27 +902,82 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         int bm = repair_tile_rows(g0, sbw0, (int)max_rows);
         // chunks of more than one row tile: a 2-CTA cluster per chunk
         bool cluster = max_rows > (size_t)bm && max_rows <= (size_t)bm * RP_MAX_TILES_PER_CHUNK;
+        int split = 0, split_sms = 0;  // > 0: the first `split` chunks run apart (see below)
         if (!cluster && bm == 128) {
-            // One CTA per 128-row chunk is the efficient GEMM shape, but a chunk's passes then run on one SM:
-            // when the heaviest chunk alone outlasts the average load of a CTA slot (few chunks per slot, as in
-            // one GPU's row shard of a model), its rows go to a 2-CTA cluster of 64-row tiles instead.  Chunk
-            // work ~ rows x n^2 per pass; 64-row tiles run the GEMMs about 13% slower.
+            // Launch layouts, compared by their estimated makespan (chunk work ~ rows x n^2 per pass):
+            //  S  one CTA per 128-row chunk, two CTAs per SM: the efficient GEMM shape, but a chunk's passes run
+            //     on one CTA, so the heaviest chunk alone can outlast the average load of a CTA slot (few chunks
+            //     per slot, as in one GPU's row shard of a model);
+            //  P  every chunk's rows over a 2-CTA cluster of 64-row tiles (GEMMs at ~0.79 of the 128-row rate);
+            //  H  the heaviest chunks (the widest layers, first in launch order) as 2-CTA clusters whose CTAs each
+            //     own an SM (an 8-warp CTA alone runs ~1.3x faster than when it shares the SM), concurrently with
+            //     a persistent launch of the other chunks on the remaining SMs.
+            constexpr double E64 = 0.79, ALONE = 1.3;
+            std::vector<double> cw(total_chunks);
             double total_w = 0.0, max_w = 0.0;
-            for (auto& P : plans)
-                for (size_t c = 0; c < P.nchunks; c++) {
-                    const double w = (double)std::min(P.rc, P.d_out - c * P.rc) * (double)P.n * (double)P.n;
-                    total_w += w;
-                    max_w = std::max(max_w, w);
-                }
+            for (size_t i = 0; i < total_chunks; i++) {
+                const ChunkInfo& c = chunks_l[i];
+                cw[i] = (double)c.rows * (double)c.n * (double)c.n;
+                total_w += cw[i];
+                max_w = std::max(max_w, cw[i]);
+            }
             const double slots = 2.0 * sms;
             const double t_single = std::max(total_w / slots, max_w);
-            const double t_pair = std::max(total_w / slots, 0.5 * max_w) / 0.87;
-            if (t_pair < t_single) {
+            const double t_pair = std::max(total_w / (slots * E64), 0.5 * max_w / E64);
+            double best = std::min(t_single, t_pair);
+            int mode = t_pair < t_single ? 1 : 0;
+            // heavy prefix: the chunks of the widest layers
+            size_t nh = 0;
+            while (nh < total_chunks && chunks_l[nh].n == chunks_l[0].n) nh++;
+            if (nh < total_chunks && max_w > total_w / slots) {
+                double wh = 0.0;
+                for (size_t i = 0; i < nh; i++) wh += cw[i];
+                const double wl = total_w - wh;
+                for (int s_h = 2; s_h < sms; s_h += 2) {
+                    if ((size_t)s_h > 2 * nh) break;
+                    const double th = std::max(max_w / (2.0 * E64 * ALONE), wh / (s_h * E64 * ALONE));
+                    const double tl = wl / (2.0 * (sms - s_h));
+                    const double t = std::max(th, tl);
+                    if (t < best) {
+                        best = t;
+                        mode = 2;
+                        split = (int)nh;
+                        split_sms = s_h;
+                    }
+                }
+            }
+            if (mode == 1) {
                 bm = 64;
                 cluster = true;
             }
+            if (mode != 2) split = 0;
         }
-        if (cluster)
+        if (split > 0) {
+            // heavy chunks on `st` (one CTA per SM), the others on a second stream, joined on `st`
+            int* counter_l = nullptr;
+            if ((rc = ar.alloc(&counter_l, 1))) return rc;
+            cudaStream_t ls = pool_stream(0);
+            cudaEvent_t fork = nullptr, join = nullptr;
+            CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&fork, cudaEventDisableTiming));
+            CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&join, cudaEventDisableTiming));
+            cudaEventRecord(fork, st);
+            cudaStreamWaitEvent(ls, fork, 0);
+            size_t maxsm = 0;
+            {
+                int dev = 0, v = 0;
+                cudaGetDevice(&dev);
+                cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+                maxsm = (size_t)v;
+            }
+            rc = launch_repair_cluster(chunks_dev, split, rp, g0, sbw0, 64, counter, st, split_sms, maxsm / 2 + 4096);
+            if (!rc)
+                rc = launch_repair_persistent(chunks_dev + split, (int)total_chunks - split, rp, g0, sbw0, 128,
+                                              counter_l, ls, 2 * (sms - split_sms));
+            cudaEventRecord(join, ls);
+            cudaStreamWaitEvent(st, join, 0);
+            cudaEventDestroy(fork);
+            cudaEventDestroy(join);
+        } else if (cluster)
             rc = launch_repair_cluster(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);
         else
             rc = launch_repair_persistent(chunks_dev, (int)total_chunks, rp, g0, sbw0, bm, counter, st);

@@ -126,11 +126,13 @@ size_t repair_smem_bytes(int g, int sbw, int bm);
 int repair_tile_rows(int g, int sbw, int max_rows);
 constexpr int RP_MAX_TILES_PER_CHUNK = 32;  // mode C keeps at most this many tile partials per chunk
 // All passes + final refit of every chunk in one launch (chunks taken from *counter_dev, in array order).
+// max_ctas > 0 caps the grid (the launch shares the GPU with another one).
 int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
-                             int* counter_dev, cudaStream_t st);
+                             int* counter_dev, cudaStream_t st, int max_ctas = 0);
 // Same with a 2-CTA cluster per chunk (chunks of more than one and at most RP_MAX_TILES_PER_CHUNK tiles).
+// smem_floor > 0 reserves that much shared memory per CTA so that no other CTA shares its SM.
 int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
-                          int* counter_dev, cudaStream_t st);
+                          int* counter_dev, cudaStream_t st, int max_ctas = 0, size_t smem_floor = 0);
 
 // ---------------------------------------------------------------------------------------------------------
 // Generic f32 GEMM with the fixed order: C = alpha*A*B (+ beta*C), A row-major or transposed (gemm.cu)

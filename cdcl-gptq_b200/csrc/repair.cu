@@ -135,19 +135,20 @@ int launch_repair_pass(const ChunkInfo* chunks_dev, const SliceItem* slices_dev,
 }
 
 int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
-                          int* counter_dev, cudaStream_t st) {
+                          int* counter_dev, cudaStream_t st, int max_ctas, size_t smem_floor) {
     if (nchunks == 0) return 0;
     size_t smem = repair_smem_bytes(g, sbw, bm);
-    return bm == 128 ? launch_repair_cluster_bm128(chunks_dev, nchunks, rp, smem, counter_dev, st)
-                     : launch_repair_cluster_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st);
+    if (smem < smem_floor) smem = smem_floor;  // reserved, unused: keeps other CTAs off the SM
+    return bm == 128 ? launch_repair_cluster_bm128(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas)
+                     : launch_repair_cluster_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas);
 }
 
 int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
-                             int* counter_dev, cudaStream_t st) {
+                             int* counter_dev, cudaStream_t st, int max_ctas) {
     if (nchunks == 0) return 0;
     size_t smem = repair_smem_bytes(g, sbw, bm);
-    return bm == 128 ? launch_repair_persistent_bm128(chunks_dev, nchunks, rp, smem, counter_dev, st)
-                     : launch_repair_persistent_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st);
+    return bm == 128 ? launch_repair_persistent_bm128(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas)
+                     : launch_repair_persistent_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas);
 }
 
 // ---------------------------------------------------------------------------------------------------------

@@ -678,15 +678,17 @@ static inline int sm_count() {
     return sms;
 }
 
+// max_ctas > 0 caps the grid (the launch then shares the GPU with another one).
 template <int BM>
 static int launch_cluster_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                             int* counter_dev, cudaStream_t st) {
+                             int* counter_dev, cudaStream_t st, int max_ctas = 0) {
     int rc = set_repair_smem((const void*)repair_cluster_kernel<BM>, smem);
     if (rc) return rc;
     int per_sm = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_cluster_kernel<BM>, 256, smem);
     if (per_sm < 1) per_sm = 1;
     int clusters = sm_count() * per_sm / 2;
+    if (max_ctas > 0 && clusters > max_ctas / 2) clusters = max_ctas / 2;
     if (clusters > nchunks) clusters = nchunks;
     if (clusters < 1) clusters = 1;
     CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
@@ -697,13 +699,14 @@ static int launch_cluster_bm(const ChunkInfo* chunks_dev, int nchunks, const Rep
 
 template <int BM>
 static int launch_persistent_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                                int* counter_dev, cudaStream_t st) {
+                                int* counter_dev, cudaStream_t st, int max_ctas = 0) {
     int rc = set_repair_smem((const void*)repair_persistent_kernel<BM>, smem);
     if (rc) return rc;
     int per_sm = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, repair_persistent_kernel<BM>, 256, smem);
     if (per_sm < 1) per_sm = 1;
     int grid = sm_count() * per_sm;
+    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
     if (grid > nchunks) grid = nchunks;
     CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
     CDCLQ_LAUNCH(repair_persistent_kernel<BM>, grid, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
@@ -726,15 +729,15 @@ static int persistent_ctas_per_sm(size_t smem) {
     return per_sm;
 }
 
-// Per-BM entry points (repair_bm64.cu, repair_bm128.cu).
+// Per-BM entry points (repair_bm64.cu, repair_bm128.cu); max_ctas > 0 caps the grid.
 int launch_repair_persistent_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                                  int* counter_dev, cudaStream_t st);
+                                  int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_cluster_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                               int* counter_dev, cudaStream_t st);
+                               int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_persistent_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                                   int* counter_dev, cudaStream_t st);
+                                   int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_cluster_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
-                                int* counter_dev, cudaStream_t st);
+                                int* counter_dev, cudaStream_t st, int max_ctas);
 int repair_persistent_ctas_per_sm_bm128(size_t smem);
 
 }  // namespace cdclq

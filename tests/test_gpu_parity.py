@@ -209,3 +209,52 @@ def test_numpy_reference_fixtures_on_gpu(gpu):
         assert np.array_equal(ql.zeros, z["oracle_zeros"])
         assert st.loss_gptq == float(z["oracle_loss"])
         assert float(np.mean(ql.codes == z["ref_codes"])) >= 0.995
+
+
+def test_batch_split_heavy_and_light_chunks(gpu):
+    """Eight heavy chunks (d_in 512) beside 300 light ones (d_in 64) in one batch: the heavy chunks run as 2-CTA
+    clusters that own their SMs, concurrently with a persistent launch of the light chunks.  Same results as the
+    oracle per layer."""
+    import ctypes
+
+    import cdclq
+    from cdclq.abi import CBatchInput, CBatchLayer, CLayerStats
+
+    cfg = Config(group=32, block=64, sub_block=32, row_chunk=128, passes=3)
+    ns = [512, 64]
+    hs = [orc.problem(1, n, 1500, 90 + i)[1] for i, n in enumerate(ns)]
+    specs = [(0, 1024), (1, 38400)]
+    ws = [orc.rng_normal(95 + i, d * ns[inp], 0.04).reshape(d, ns[inp]) for i, (inp, d) in enumerate(specs)]
+    ins = (CBatchInput * len(ns))()
+    keep = []
+    for i, h in enumerate(hs):
+        hh = np.ascontiguousarray(h, np.float32)
+        keep.append(hh)
+        ins[i].h = hh.ctypes.data
+        ins[i].n = ns[i]
+    lys = (CBatchLayer * len(specs))()
+    outs, stats = [], [CLayerStats() for _ in specs]
+    for i, (inp, d) in enumerate(specs):
+        n = ns[inp]
+        ng = (n + 31) // 32
+        o = dict(perm=np.zeros(n, np.uint32), gbits=np.zeros(ng, np.uint8), codes=np.zeros((d, n), np.uint8),
+                 scales=np.zeros((d, ng), np.float32), zeros=np.zeros((d, ng), np.float32))
+        outs.append(o)
+        ww = np.ascontiguousarray(ws[i], np.float32)
+        keep.append(ww)
+        lys[i].w = ww.ctypes.data
+        lys[i].d_out = d
+        lys[i].input = inp
+        for k in ("perm", "gbits", "codes", "scales", "zeros"):
+            setattr(lys[i], k, o[k].ctypes.data)
+        lys[i].stats = ctypes.pointer(stats[i])
+    c = cfg.to_c()
+    cdclq._lib.check(cdclq.lib().cdclq_quantize_batch(ins, len(ns), lys, len(specs), ctypes.byref(c), 0, None))
+    for i, (inp, d) in enumerate(specs):
+        qb, sb = orc.quantize_layer(ws[i], d, ns[inp], hs[inp], None, "x", cfg)
+        o = outs[i]
+        assert np.array_equal(o["codes"], qb.codes) and np.array_equal(o["scales"], qb.scales)
+        assert np.array_equal(o["zeros"], qb.zeros) and np.array_equal(o["perm"], qb.perm)
+        assert stats[i].loss_gptq == sb.loss_gptq
+        assert abs(stats[i].loss_final - sb.loss_final) <= 1e-9 * sb.loss_final
+        assert stats[i].code_updates == sb.code_updates

@@ -17,14 +17,31 @@ def test_shard_rows_cover_every_row_in_whole_chunks():
     for d_out in (1, 64, 127, 128, 129, 256, 1000, 2048, 5632):
         for rc in (16, 100, 128):
             for world in (1, 2, 3, 4, 8):
-                spans = [shard_rows(d_out, rc, r, world) for r in range(world)]
-                assert spans[0][0] == 0 and spans[-1][1] == d_out
-                for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
-                    assert a1 == b0  # contiguous, in rank order
-                for r0, r1 in spans:
-                    assert r0 <= r1
-                    assert r0 % rc == 0  # a shard starts on a row-chunk boundary
-                    assert r1 % rc == 0 or r1 == d_out
+                for rotate in (0, 1, 5):
+                    spans = sorted(shard_rows(d_out, rc, r, world, rotate) for r in range(world))
+                    assert spans[0][0] == 0 and spans[-1][1] == d_out
+                    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+                        assert a1 == b0  # the ranks' ranges tile the rows without overlap
+                    for r0, r1 in spans:
+                        assert r0 <= r1
+                        assert r0 % rc == 0  # a shard starts on a row-chunk boundary
+                        assert r1 % rc == 0 or r1 == d_out
+
+
+def test_rotated_shards_balance_a_model():
+    """TinyLlama-shaped layers: with the per-layer rotation no rank holds more than one row chunk per layer
+    group above the mean."""
+    from cdclq.pipeline import shard_rows
+
+    block = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (5632, 2048), (5632, 2048), (2048, 5632)]
+    layers = block * 22
+    for world in (2, 4, 8):
+        load = [0] * world
+        for li, (d_out, d_in) in enumerate(layers):
+            for r in range(world):
+                r0, r1 = shard_rows(d_out, 128, r, world, rotate=li)
+                load[r] += (r1 - r0) * d_in * d_in
+        assert max(load) <= 1.06 * (sum(load) / world), (world, max(load) / (sum(load) / world))
 
 
 def test_factorisation_owners_balance_n_cubed():
