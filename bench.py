@@ -337,6 +337,147 @@ def run_syrk_bench(args, torch):
         torch.cuda.empty_cache()
 
 
+L7_HIDDEN, L7_INTER, L7_LAYERS = 4096, 11008, 32
+L7_BLOCK = [("q_proj", L7_HIDDEN, L7_HIDDEN, "attn"), ("k_proj", L7_HIDDEN, L7_HIDDEN, "attn"),
+            ("v_proj", L7_HIDDEN, L7_HIDDEN, "attn"), ("o_proj", L7_HIDDEN, L7_HIDDEN, "o"),
+            ("gate_proj", L7_INTER, L7_HIDDEN, "mlp"), ("up_proj", L7_INTER, L7_HIDDEN, "mlp"),
+            ("down_proj", L7_HIDDEN, L7_INTER, "down")]
+L7_INPUT_DIM = {"attn": L7_HIDDEN, "o": L7_HIDDEN, "mlp": L7_HIDDEN, "down": L7_INTER}
+
+
+def run_llama2_7b(args, torch, rank, world):
+    """The north-star configuration end to end: a Llama-2-7B-shaped model (32 layers, 6.48e9
+    bf16-valued weights N(0, 0.02^2) with 0.1 % of input columns x10), every distinct input's Hessian accumulated
+    on the GPU by the tensor-core SYRK from 262144 seeded bf16 activations (configs[0] channel profile), then
+    CDCL quantization at `--bits` with group 64, --mse-grid, refine-frac 0.25, row chunk 128.
+
+    Timed (CUDA events, max over ranks): the Hessian accumulations and the quantization.  Not timed: generating
+    the synthetic activations and weights.  N > 1: the distinct inputs are assigned to ranks (longest processing
+    time on n^2); each owner accumulates its Hessians over all tokens and broadcasts them (f32, NCCL); the
+    quantization is cdclq.pipeline.ModelBatch (row shards, factorisations spread, U broadcast).  One GPU: the
+    layers go through the engine in two groups of sixteen blocks (memory)."""
+    import cdclq
+    from cdclq import linalg
+    from cdclq.abi import Config
+    from cdclq.pipeline import ModelBatch, assign_factorisations, shard_rows
+
+    cdclq.lib()
+    dev = "cuda"
+    cfg = Config(bits=args.bits, group=64, mse_grid=True, refine_frac=0.25, row_chunk=ROW_CHUNK)
+    st = torch.cuda.current_stream()
+    layers, inputs = [], []
+    for b in range(L7_LAYERS):
+        idx = {}
+        for kind in ("attn", "o", "mlp", "down"):
+            idx[kind] = len(inputs)
+            inputs.append(("model.layers.%d.%s" % (b, kind), L7_INPUT_DIM[kind]))
+        for name, d_out, d_in, kind in L7_BLOCK:
+            layers.append(("model.layers.%d.%s" % (b, name), d_out, d_in, idx[kind]))
+    total_weights = sum(l[1] * l[2] for l in layers)
+
+    def weight(i, d_out, n, rows=None):
+        g = torch.Generator(device=dev)
+        g.manual_seed(90000 + i)
+        w = torch.randn(d_out, n, generator=g, device=dev) * 0.02
+        gc = torch.Generator(device="cpu")
+        gc.manual_seed(91000 + i)
+        cols = torch.randperm(n, generator=gc)[:max(1, n // 1000)].to(dev)
+        w[:, cols] *= 10.0
+        if rows is not None:
+            w = w[rows[0]:rows[1]]
+        return w.to(torch.bfloat16).float().contiguous()
+
+    def tokens(i, n):
+        scale = channel_profile(n, 3000 + i, torch, dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(4000 + i)
+        return (torch.randn(TOKENS, n, generator=g, device=dev) * scale).to(torch.bfloat16).contiguous()
+
+    ev_ms = 0.0  # timed device work on this rank
+    phase_ms = {"hessians": 0.0, "hessian_broadcast": 0.0, "quantization": 0.0}
+
+    def timed(fn, phase):
+        nonlocal ev_ms
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        out = fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ev_ms += e0.elapsed_time(e1)
+        phase_ms[phase] += e0.elapsed_time(e1)
+        return out
+
+    # ---- Hessians: owners accumulate, then every rank receives them
+    owner = assign_factorisations([n for (_, n) in inputs], world, power=2) if world > 1 else [0] * len(inputs)
+    if world > 1:
+        torch.distributed.barrier()
+    H = [None] * len(inputs)
+    for i, (_, n) in enumerate(inputs):
+        if owner[i] == rank:
+            x = tokens(i, n)
+            h64 = torch.zeros(n, n, dtype=torch.float64, device=dev)
+            timed(lambda: linalg.gram_accumulate_bf16_device(x, h64, lower_only=False, stream=st.cuda_stream),
+                  "hessians")
+            H[i] = timed(lambda: h64.float(), "hessians")
+            del x, h64
+        else:
+            H[i] = torch.empty(n, n, dtype=torch.float32, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        def bcast():
+            for i, h in enumerate(H):
+                dist.broadcast(h, src=owner[i])
+        timed(bcast, "hessian_broadcast")
+    torch.cuda.empty_cache()
+
+    # ---- quantization
+    stats = []
+    if world > 1:
+        W = []
+        for i, (_, d_out, n, _) in enumerate(layers):
+            r = shard_rows(d_out, ROW_CHUNK, rank, world, rotate=i)
+            W.append(weight(i, d_out, n, r) if r[1] > r[0] else None)
+        torch.distributed.barrier()
+        b = ModelBatch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True, w_sharded=True)
+        timed(lambda: b.run(st.cuda_stream), "quantization")
+        stats = list(b.stats)
+        del W, b
+    else:
+        per = 16 * len(L7_BLOCK)
+        for l0 in range(0, len(layers), per):
+            part = layers[l0:l0 + per]
+            W = [weight(l0 + j, d_out, n) for j, (_, d_out, n, _) in enumerate(part)]
+            b = ModelBatch(torch, part, inputs, H, W, cfg, on_device=True)
+            timed(lambda: b.run(st.cuda_stream), "quantization")
+            stats += list(b.stats)
+            del W, b
+            torch.cuda.empty_cache()
+    ms = ev_ms
+    loss = [sum(s.loss_gptq for s in stats), sum(s.loss_final for s in stats)]
+    phases = [phase_ms[k] for k in ("hessians", "hessian_broadcast", "quantization")]
+    if world > 1:
+        t = torch.tensor([ms] + phases, dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, phases = float(t[0]), [float(v) for v in t[1:]]
+        lt = torch.tensor(loss, dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(lt)
+        loss = [float(lt[0]), float(lt[1])]
+    if rank == 0:
+        print(json.dumps({
+            "metric": "seconds per model quantized incl. Hessian accumulation and CDCL repair (north-star config)",
+            "value": ms * 1e-3, "unit": "s", "higher_is_better": False, "n_gpus": world,
+            "weights_per_s": total_weights / (ms * 1e-3), "target_s": 60.0, "target_gpus": 8,
+            "config": {"workload": "Llama-2-7B-shaped model (configs[3]): 32 layers, 224 linear layers, %.3g weights, "
+                                   "128 Hessians accumulated on the GPU from 262144 bf16 tokens each" % total_weights,
+                       "bits": args.bits, "group": 64, "mse_grid": True, "refine_frac": 0.25, "row_chunk": ROW_CHUNK},
+            "timed": "tensor-core Hessian accumulation + quantization (activation and weight generation excluded)",
+            "phases_s_max_over_ranks": {"hessians": phases[0] * 1e-3, "hessian_broadcast": phases[1] * 1e-3,
+                                        "quantization": phases[2] * 1e-3},
+            "loss_gptq": loss[0], "loss_final": loss[1], "data": "synthetic (seeded)",
+        }), flush=True)
+
+
 def workload_config(cfg):
     return {"workload": "TinyLlama-1.1B-shaped model (configs[1]): 22 decoder layers, 154 linear layers, "
                         "9.69e8 bf16-valued weights, 88 Hessians from 262144 seeded tokens",
@@ -357,6 +498,9 @@ def main():
     ap.add_argument("--kernel", default="model", choices=["model", "syrk"],
                     help="syrk: time the bf16 tensor-core Hessian accumulation alone (one JSON line per width)")
     ap.add_argument("--syrk-widths", default="2048,4096,5632,11008", help="--kernel syrk: channel counts n")
+    ap.add_argument("--model", default="tinyllama", choices=["tinyllama", "llama2-7b"],
+                    help="llama2-7b: the north-star configuration (configs[3]) end to end, one extra JSON line")
+    ap.add_argument("--bits", type=int, default=4, help="--model llama2-7b: code width (4 or 2)")
     ap.add_argument("--syrk-tokens", type=int, default=TOKENS, help="--kernel syrk: tokens per Hessian")
     args = ap.parse_args()
 
@@ -383,6 +527,11 @@ def main():
     if args.kernel == "syrk":
         if rank == 0:
             run_syrk_bench(args, torch)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if args.model == "llama2-7b":
+        run_llama2_7b(args, torch, rank, world)
         if world > 1:
             torch.distributed.destroy_process_group()
         return

@@ -36,15 +36,16 @@ def shard_rows(d_out, row_chunk, rank, world, rotate=0):
     return min(c0 * row_chunk, d_out), min(c1 * row_chunk, d_out)
 
 
-def assign_factorisations(ns, world):
-    """Owner rank of each distinct input: longest-processing-time scheduling on the n^3 cost of its
-    factorisation (largest first, ties by index), each to the least-loaded rank (ties to the lowest rank)."""
+def assign_factorisations(ns, world, power=3):
+    """Owner rank of each distinct input: longest-processing-time scheduling on the n^power cost of its work
+    (n^3: Cholesky + triangular inverse; n^2: a Hessian accumulation over a fixed token count), largest first,
+    ties by index, each to the least-loaded rank (ties to the lowest rank)."""
     owner = [0] * len(ns)
     load = [0.0] * world
     for i in sorted(range(len(ns)), key=lambda i: (-ns[i], i)):
         r = min(range(world), key=lambda r: (load[r], r))
         owner[i] = r
-        load[r] += float(ns[i]) ** 3
+        load[r] += float(ns[i]) ** power
     return owner
 
 
@@ -63,10 +64,13 @@ class ModelBatch:
     layers: [(name, d_out, d_in, input index)]; inputs: [(name, n)]; H: per input an n x n f32 tensor; W: per
     layer a d_out x d_in f32 tensor (original column order).  All tensors on the device (on_device=True) or
     all in (pinned) host memory (on_device=False, copies inside the library).  With world > 1 the rank keeps
-    the rows shard_rows() gives it, and `run` needs torch.distributed initialised (NCCL).
+    the rows shard_rows() gives it, and `run` needs torch.distributed initialised (NCCL).  With w_sharded=True
+    each W entry holds only this rank's rows (shard_rows(d_out, cfg.row_chunk, rank, world, rotate=layer index))
+    and layers without rows on this rank may be None.
     """
 
-    def __init__(self, torch, layers, inputs, H, W, cfg, rank=0, world=1, on_device=True, distribute_factors=True):
+    def __init__(self, torch, layers, inputs, H, W, cfg, rank=0, world=1, on_device=True, distribute_factors=True,
+                 w_sharded=False):
         self.torch = torch
         self.cfg = cfg
         self.rank, self.world = rank, world
@@ -96,7 +100,9 @@ class ModelBatch:
         for i, (name, d_out, d_in, inp, w, r0, r1) in enumerate(rows):
             ng = num_groups(cfg, d_in)
             rs = r1 - r0
-            wv = w[r0:r1]
+            wv = w if w_sharded else w[r0:r1]
+            if tuple(wv.shape) != (rs, d_in):
+                raise ValueError("%s: weight rows %s, expected %s" % (name, tuple(wv.shape), (rs, d_in)))
             self.keep.append(wv)
             o = dict(perm=np.zeros(d_in, np.uint32), gbits=np.zeros(ng, np.uint8),
                      codes=torch.empty(rs, d_in, dtype=torch.uint8, device=dev, pin_memory=not on_device),
