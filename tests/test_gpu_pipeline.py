@@ -101,3 +101,28 @@ def test_row_shards_concatenate_to_the_full_result(gpu):
                 assert np.array_equal(np.concatenate([o[k] for _, o in rows]), ref[li][k]), (name, world, k)
             for _, o in rows:
                 assert np.array_equal(o["perm"], ref[li]["perm"])
+
+
+def test_rank_local_weight_shards_give_the_same_rows(gpu):
+    """w_sharded=True: each rank passes only its own rows of W (the multi-GPU bench generates them per rank)."""
+    import torch
+
+    from cdclq.pipeline import ModelBatch, shard_rows
+
+    layers, inputs, hs, ws = model(torch, "cuda")
+    world = 2
+    for rank in range(world):
+        a = ModelBatch(torch, layers, inputs, hs, ws, CFG, rank=rank, world=world, distribute_factors=False)
+        a.run(0)
+        wl = []
+        for li, (_, d_out, _, _) in enumerate(layers):
+            r0, r1 = shard_rows(d_out, CFG.row_chunk, rank, world, rotate=li)
+            wl.append(ws[li][r0:r1].clone() if r1 > r0 else None)
+        b = ModelBatch(torch, layers, inputs, hs, wl, CFG, rank=rank, world=world, distribute_factors=False,
+                       w_sharded=True)
+        b.run(0)
+        torch.cuda.synchronize()
+        assert a.names == b.names and a.shards == b.shards
+        assert_same(outputs(a), outputs(b))
+    with pytest.raises(ValueError):
+        ModelBatch(torch, layers, inputs, hs, ws, CFG, rank=0, world=2, distribute_factors=False, w_sharded=True)

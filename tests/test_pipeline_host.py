@@ -61,6 +61,19 @@ def test_factorisation_owners_balance_n_cubed():
     assert sorted(down[:8]) == list(range(8))
 
 
+def test_hessian_owners_balance_n_squared():
+    """Hessian accumulations (cost n^2 at a fixed token count) of the Llama-2-7B-shaped model: 96 inputs of
+    4096 and 32 of 11008 channels spread by LPT on n^2 within one job of the mean."""
+    from cdclq.pipeline import assign_factorisations
+
+    ns = [4096, 4096, 4096, 11008] * 32
+    for world in (2, 4, 8):
+        owner = assign_factorisations(ns, world, power=2)
+        load = [sum(float(n) ** 2 for n, o in zip(ns, owner) if o == r) for r in range(world)]
+        assert max(load) <= sum(load) / world + 11008.0 ** 2 + 1.0
+        assert set(owner) == set(range(world))
+
+
 def test_prepared_entry_points_reject_a_weight_dependent_permutation():
     import cdclq
     from cdclq.abi import CBatchInput, Config
