@@ -433,6 +433,13 @@ def run_llama2_7b(args, torch, rank, world):
 
     # ---- quantization
     stats = []
+    eng = {k: 0.0 for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair", "ms_final")}
+
+    def add_profile():
+        prof = cdclq._lib.last_run_profile()
+        for k in eng:
+            eng[k] += prof[k]
+
     if world > 1:
         W = []
         for i, (_, d_out, n, _) in enumerate(layers):
@@ -441,6 +448,7 @@ def run_llama2_7b(args, torch, rank, world):
         torch.distributed.barrier()
         b = ModelBatch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True, w_sharded=True)
         timed(lambda: b.run(st.cuda_stream), "quantization")
+        add_profile()
         stats = list(b.stats)
         del W, b
     else:
@@ -450,6 +458,7 @@ def run_llama2_7b(args, torch, rank, world):
             W = [weight(l0 + j, d_out, n) for j, (_, d_out, n, _) in enumerate(part)]
             b = ModelBatch(torch, part, inputs, H, W, cfg, on_device=True)
             timed(lambda: b.run(st.cuda_stream), "quantization")
+            add_profile()
             stats += list(b.stats)
             del W, b
             torch.cuda.empty_cache()
@@ -472,6 +481,7 @@ def run_llama2_7b(args, torch, rank, world):
                                    "128 Hessians accumulated on the GPU from 262144 bf16 tokens each" % total_weights,
                        "bits": args.bits, "group": 64, "mse_grid": True, "refine_frac": 0.25, "row_chunk": ROW_CHUNK},
             "timed": "tensor-core Hessian accumulation + quantization (activation and weight generation excluded)",
+            "engine_phases_ms_rank0": eng,
             "phases_s_max_over_ranks": {"hessians": phases[0] * 1e-3, "hessian_broadcast": phases[1] * 1e-3,
                                         "quantization": phases[2] * 1e-3},
             "loss_gptq": loss[0], "loss_final": loss[1], "data": "synthetic (seeded)",

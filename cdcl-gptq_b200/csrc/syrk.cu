@@ -5,16 +5,17 @@
 // chunk's sum into the f64 Hessian.  Here each 2048-token chunk is one f32 tensor-core accumulation in tensor
 // memory (bf16 x bf16 products are exact in f32; the summation order inside the tensor core differs from a
 // sequential sum, so this path agrees with the f32 path to f32 accumulation error, not bit for bit), then the
-// epilogue widens the chunk into the f64 Hessian in global memory, as the reference does.
+// epilogue widens the chunk into the f64 Hessian in global memory, as the reference does.  Only the lower
+// triangle is accumulated; when the full matrix is wanted, one pass at the end copies it onto the upper triangle
+// (the reference's H is symmetric: both triangles receive the same sums in the same order).
 //
 // One CTA computes output tiles D[p][q] = sum_t X[t][p] X[t][q] of 128 (p) x 256 (q) channels with q >= p
 // somewhere in the tile, tiles taken round-robin by a persistent grid.  Per 64-token K block, TMA brings the
-// p block (2 boxes of 64 channels x 64 tokens) and the q block (4 boxes) into a 4-stage shared-memory ring
+// p block (2 boxes of 64 channels x 64 tokens) and the q block (4 boxes) into a 3-stage shared-memory ring
 // (128-byte swizzle, MN-major for the MMA: channels are contiguous in X); one thread issues four
 // 128x256x16 bf16 MMAs per block into a tensor-memory accumulator.  Two accumulators (2 x 256 columns) let the
 // eight epilogue warps widen chunk c while the MMAs of chunk c+1 run.  The epilogue thread of TMEM lane p adds
-// D[p][q] into H[q][p] (lanes along a row of H: coalesced) and, unless only the lower triangle is wanted,
-// into H[p][q] for q > p, so H stays exactly symmetric.
+// D[p][q] into H[q][p] for q >= p (lanes along a row of H: coalesced).
 //
 // Roles: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4).. and columns 128(w/4)..), warp 8 TMA producer,
 // warp 9 MMA issuer and TMEM owner.  Every wait on an mbarrier is bounded: on timeout the kernel records an error, leaves its loops,
@@ -42,7 +43,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // 48 KB
 constexpr int EPI_WARPS = 8;     // two per TMEM lane quadrant, each taking half of the tile's columns
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
 constexpr int TMEM_COLS = 2 * BNQ;                  // two accumulators
-constexpr size_t SMEM_BYTES = (size_t)NS * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr size_t smem_bytes(int ns) { return (size_t)ns * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */; }
 constexpr int WAIT_LIMIT = 1 << 24;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -160,7 +161,9 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_q, int& pb, int&
     qb = (pb >> 1) + tile;
 }
 
+template <int NSTAGES>
 __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
+    constexpr int NS = NSTAGES;  // shared-memory stages
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + NS * STAGE_BYTES);
@@ -168,7 +171,6 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
     uint64_t* accf = empty + NS;
     uint64_t* acce = accf + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
-    __shared__ float tr[EPI_WARPS][32 * 33];  // epilogue transposes (one 32 x 32 block per warp)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int* err = P.err;
 
@@ -221,7 +223,8 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                         tma_load_2d(st, &tmap, p0, y, &full[s]);
                         tma_load_2d(st + BOX_BYTES, &tmap, p0 + 64, y, &full[s]);
 #pragma unroll
-                        for (int h = 0; h < 4; h++) tma_load_2d(st + A_BYTES + h * BOX_BYTES, &tmap, q0 + 64 * h, y, &full[s]);
+                        for (int h = 0; h < 4; h++)
+                            tma_load_2d(st + A_BYTES + h * BOX_BYTES, &tmap, q0 + 64 * h, y, &full[s]);
                     }
                 }
             }
@@ -272,7 +275,6 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
         }
     } else {
         // ---------------- epilogue: warps 0..7; TMEM lanes 32*(warp%4) .., columns 128*(warp/4) ..
-        float* trw = tr[warp];
         const int quad = warp & 3, half = warp >> 2;
         int acc = 0;
         bool ok = true;
@@ -311,40 +313,18 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                         }
                         continue;
                     }
-                    // lower triangle: H[q][p] += D[p][q] (lanes along a row of H).  All 32 loads are issued
-                    // before any store, so the read-modify-writes overlap instead of waiting on each other.
-                    {
-                        double old[32];
+                    // H[q][p] += D[p][q] for q >= p (lanes along a row of H).  All 32 loads are issued before any
+                    // store, so the read-modify-writes overlap instead of waiting on each other.
+                    double old[32];
 #pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const int q = qc0 + i;
-                            old[i] = (p < n && q < n && q >= p) ? P.h[(int64_t)q * n + p] : 0.0;
-                        }
-#pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const int q = qc0 + i;
-                            if (p < n && q < n && q >= p) P.h[(int64_t)q * n + p] = __dadd_rn(old[i], (double)v[i]);
-                        }
+                    for (int i = 0; i < 32; i++) {
+                        const int q = qc0 + i;
+                        old[i] = (p < n && q < n && q >= p) ? P.h[(int64_t)q * n + p] : 0.0;
                     }
-                    if (!P.lower_only) {
-                        // upper triangle: H[p][q] += D[p][q] for q > p, through a transpose so lanes run along q
 #pragma unroll
-                        for (int i = 0; i < 32; i++) trw[i * 33 + lane] = v[i];
-                        __syncwarp();
-                        const int q = qc0 + lane;
-                        double old[32];
-#pragma unroll
-                        for (int r = 0; r < 32; r++) {
-                            const int pr = prow0 + r;
-                            old[r] = (pr < n && q < n && q > pr) ? P.h[(int64_t)pr * n + q] : 0.0;
-                        }
-#pragma unroll
-                        for (int r = 0; r < 32; r++) {
-                            const int pr = prow0 + r;
-                            if (pr < n && q < n && q > pr)
-                                P.h[(int64_t)pr * n + q] = __dadd_rn(old[r], (double)trw[lane * 33 + r]);
-                        }
-                        __syncwarp();
+                    for (int i = 0; i < 32; i++) {
+                        const int q = qc0 + i;
+                        if (p < n && q < n && q >= p) P.h[(int64_t)q * n + p] = __dadd_rn(old[i], (double)v[i]);
                     }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -365,7 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
 
 namespace syrk {
 
-// Split tiles: H[q][p] += partial_0 + partial_1 + ... (segments in order), and the mirror for q > p.
+// Split tiles: H[q][p] += partial_0 + partial_1 + ... (segments in order), q >= p.
 // Block = 128 threads (p within the tile), grid = (tiles, 256 / 32 column groups).
 __global__ void __launch_bounds__(128) syrk_reduce_kernel(const Params P) {
     const int tile = blockIdx.x;
@@ -377,14 +357,28 @@ __global__ void __launch_bounds__(128) syrk_reduce_kernel(const Params P) {
         const int q = qb * BNQ + ql;
         if (q >= n || q < p) continue;
         double lo = P.h[(int64_t)q * n + p];
-        double up = (!P.lower_only && q > p) ? P.h[(int64_t)p * n + q] : 0.0;
-        for (int sg = 0; sg < P.nseg; sg++) {
-            const double v = P.scratch[((int64_t)sg * P.ntiles + tile) * (BMP * BNQ) + (int64_t)ql * BMP + pl];
-            lo = __dadd_rn(lo, v);
-            up = __dadd_rn(up, v);
-        }
+        for (int sg = 0; sg < P.nseg; sg++)
+            lo = __dadd_rn(lo, P.scratch[((int64_t)sg * P.ntiles + tile) * (BMP * BNQ) + (int64_t)ql * BMP + pl]);
         P.h[(int64_t)q * n + p] = lo;
-        if (!P.lower_only && q > p) P.h[(int64_t)p * n + q] = up;
+    }
+}
+
+// Full-matrix result: the upper triangle becomes the lower one's mirror, H[p][q] = H[q][p] for q > p, through
+// 32 x 32 shared-memory tiles (reads and writes coalesced).  Grid (T, T) blocks of 32 x 8 threads, T = n / 32
+// rounded up; the blocks above the diagonal exit.
+__global__ void __launch_bounds__(256) syrk_mirror_kernel(double* h, int n) {
+    const int bi = blockIdx.y, bj = blockIdx.x;  // source tile: rows 32 bi.., columns 32 bj.. (lower: bj <= bi)
+    if (bj > bi) return;
+    __shared__ double t[32][33];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    for (int r = ty; r < 32; r += 8) {
+        const int row = bi * 32 + r, col = bj * 32 + tx;
+        if (row < n && col < n) t[r][tx] = h[(int64_t)row * n + col];
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int row = bj * 32 + r, col = bi * 32 + tx;  // destination H[row][col] = H[col][row], col > row
+        if (row < n && col < n && col > row) h[(int64_t)row * n + col] = t[tx][r];
     }
 }
 
@@ -454,7 +448,9 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&err, sizeof(int), st));
     CDCLQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     P.err = err;
-    cudaError_t e = cudaFuncSetAttribute(syrk_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    auto kern = syrk_bf16_kernel<NS>;
+    const size_t smem = smem_bytes(NS);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
         cudaFreeAsync(err, st);
         if (P.scratch) cudaFreeAsync(P.scratch, st);
@@ -462,11 +458,16 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     }
     const int items = P.ntiles * P.nseg;
     const int grid = items < sms ? items : sms;
-    CDCLQ_LAUNCH(syrk_bf16_kernel, grid, THREADS, SMEM_BYTES, st, map, P);
+    CDCLQ_LAUNCH(kern, grid, THREADS, smem, st, map, P);
     e = cudaGetLastError();
     if (e == cudaSuccess && P.nseg > 1) {
         dim3 rg(P.ntiles, BNQ / 32);
         CDCLQ_LAUNCH(syrk_reduce_kernel, rg, BMP, 0, st, P);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && !P.lower_only) {
+        const int tt = (n + 31) / 32;
+        CDCLQ_LAUNCH(syrk_mirror_kernel, dim3(tt, tt), dim3(32, 8), 0, st, h, n);
         e = cudaGetLastError();
     }
     int herr = 0;
