@@ -1453,6 +1453,8 @@ int cdclq_gram_accumulate(const float* x, const float* y, size_t t, size_t n, do
 int cdclq_gram_accumulate_bf16_device(const void* x_bf16, size_t t, size_t n, double* h, int lower_only,
                                       void* stream) {
     if (!x_bf16 || !h || n == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
+    int rc = ensure_device();  // the split-token partials come from the (caching) stream-ordered pool
+    if (rc) return rc;
     return launch_gram_bf16_tc(x_bf16, (int64_t)t, (int)n, h, lower_only, (cudaStream_t)stream);
 }
 

@@ -14,8 +14,10 @@
 // p block (2 boxes of 64 channels x 64 tokens) and the q block (4 boxes) into a 3-stage shared-memory ring
 // (128-byte swizzle, MN-major for the MMA: channels are contiguous in X); one thread issues four
 // 128x256x16 bf16 MMAs per block into a tensor-memory accumulator.  Two accumulators (2 x 256 columns) let the
-// eight epilogue warps widen chunk c while the MMAs of chunk c+1 run.  The epilogue thread of TMEM lane p adds
-// D[p][q] into H[q][p] for q >= p (lanes along a row of H: coalesced).
+// eight epilogue warps widen chunk c while the MMAs of chunk c+1 run.  D[p][q] is added into H[q][p] for
+// q >= p (TMEM lane p = one element of a row of H): off the diagonal by bulk f64 additions at L2 from a
+// shared-memory staging buffer, each tile's chunks in order (a chunk's additions complete before the next
+// chunk's are issued), so every element receives the same sums in the same order as a sequential widening.
 //
 // Roles: warps 0-7 epilogue (warp w reads TMEM lanes 32(w%4).. and columns 128(w/4)..), warp 8 TMA producer,
 // warp 9 MMA issuer and TMEM owner.  Every wait on an mbarrier is bounded: on timeout the kernel records an error, leaves its loops,
@@ -23,6 +25,7 @@
 #include <cuda.h>
 
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -43,8 +46,13 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;      // 48 KB
 constexpr int EPI_WARPS = 8;     // two per TMEM lane quadrant, each taking half of the tile's columns
 constexpr int THREADS = (EPI_WARPS + 2) * 32;
 constexpr int TMEM_COLS = 2 * BNQ;                  // two accumulators
-constexpr size_t smem_bytes(int ns) { return (size_t)ns * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */; }
+constexpr int EPI_BUF_BYTES = 16 * 32 * 8;           // 16 rows q x 32 columns p of f64: one epilogue staging buffer
+constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;  // two buffers per epilogue warp (64 KB)
+constexpr size_t smem_bytes(int ns) {
+    return (size_t)ns * STAGE_BYTES + EPI_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+}
 constexpr int WAIT_LIMIT = 1 << 24;
+constexpr int TILE_BAND = 16;    // p blocks per band of the tile order
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -85,6 +93,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+
+// Bulk f64 additions from shared memory into global memory, performed at L2 (round to nearest, as __dadd_rn).
+__device__ __forceinline__ void bulk_add_f64(double* gdst, uint32_t ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f64 [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every bulk operation of this thread has completed (its additions are performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// at most the most recent bulk group of this thread still reads its shared-memory source
+__device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory matrix descriptor of an MN-major operand with the 128-byte swizzle: 64-element (128-byte) atoms
 // along MN, `lbo` bytes apart; 8-token row groups along K, `sbo` bytes apart.
@@ -133,6 +154,7 @@ struct Params {
     int64_t t;
     int tiles_p;   // p blocks
     int tiles_q;   // q blocks
+    const int2* tiles;  // (p block, q block) of each tile in processing order
     int ntiles;    // tiles with q >= p somewhere
     int lower_only;
     int nseg;        // token segments per tile (split over CTAs when there are few tiles)
@@ -150,15 +172,10 @@ __device__ __forceinline__ void item_range(const Params& P, int item, int nchunk
 }
 
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_q, int& pb, int& qb) {
-    // tiles of p block pb: q blocks pb/2 .. tiles_q-1 (those holding some q >= p)
-    pb = 0;
-    for (; pb < 65536; pb++) {  // tile < ntiles ends the walk within the p blocks
-        const int cnt = tiles_q - (pb >> 1);
-        if (tile < cnt) break;
-        tile -= cnt;
-    }
-    qb = (pb >> 1) + tile;
+__device__ __forceinline__ void tile_coords(const Params& P, int tile, int& pb, int& qb) {
+    const int2 t = P.tiles[tile];
+    pb = t.x;
+    qb = t.y;
 }
 
 template <int NSTAGES>
@@ -166,7 +183,8 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
     constexpr int NS = NSTAGES;  // shared-memory stages
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + NS * STAGE_BYTES);
+    unsigned char* epi_base = base + NS * STAGE_BYTES;  // epilogue staging buffers
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi_base + EPI_BYTES);
     uint64_t* empty = full + NS;
     uint64_t* accf = empty + NS;
     uint64_t* acce = accf + 2;
@@ -206,7 +224,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
             for (int item = blockIdx.x; item < P.ntiles * P.nseg && ok; item += gridDim.x) {
                 int tile, c0, c1, pb, qb;
                 item_range(P, item, nchunks, tile, c0, c1);
-                tile_coords(tile, P.tiles_q, pb, qb);
+                tile_coords(P, tile, pb, qb);
                 const int p0 = pb * BMP, q0 = qb * BNQ;
                 for (int c = c0; c < c1 && ok; c++) {
                     const int64_t tok0 = (int64_t)c * CHUNK;
@@ -275,17 +293,28 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
         }
     } else {
         // ---------------- epilogue: warps 0..7; TMEM lanes 32*(warp%4) .., columns 128*(warp/4) ..
+        // Each 32 (p) x 32 (q) block of the chunk is widened to f64.  Into H, a block wholly below the diagonal goes
+        // through the warp's staging buffers into bulk additions performed at L2 (one 256-byte row segment
+        // H[q][p..p+31] per q) - against a read-modify-write from the SM this moved n = 4096 from 650 to 1000
+        // TFLOP/s; the diagonal block is added element by element (q >= p only).  With split tokens the item's
+        // partial tile in the scratch, [q - q0][p - p0], is written element by element.
         const int quad = warp & 3, half = warp >> 2;
+        double* ebuf = reinterpret_cast<double*>(epi_base + (size_t)warp * 2 * EPI_BUF_BYTES);
+        const uint32_t ebuf_s = smem_u32(ebuf);
+        int bi = 0;  // the staging buffer filled next
         int acc = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < P.ntiles * P.nseg && ok; item += gridDim.x) {
             int tile, c0, c1, pb, qb;
             item_range(P, item, nchunks, tile, c0, c1);
-            tile_coords(tile, P.tiles_q, pb, qb);
+            tile_coords(P, tile, pb, qb);
             const int p0 = pb * BMP, q0 = qb * BNQ;
             const int prow0 = p0 + quad * 32;  // this warp's 32 rows p
             const int p = prow0 + lane;
-            double* part = P.scratch + (int64_t)item * (BMP * BNQ);  // nseg > 1
+            const bool split = P.nseg > 1;
+            double* dst = split ? P.scratch + (int64_t)item * (BMP * BNQ) : P.h;
+            const int64_t ld = split ? BMP : n;
+            const int qofs = split ? q0 : 0, pofs = split ? p0 : 0;
             for (int c = c0; c < c1; c++, acc++) {
                 const int b = acc & 1;
                 if (!mbar_wait(&accf[b], (acc / 2) & 1, err)) {
@@ -293,44 +322,67 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                // the previous chunk's additions have been performed: every element receives its chunks in order
+                if (lane == 0) bulk_wait_all();
+                __syncwarp();
                 for (int cb = half * (BNQ / 64); cb < (half + 1) * (BNQ / 64); cb++) {
                     const int qc0 = q0 + cb * 32;
                     float v[32];
                     tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BNQ + cb * 32), v);
-                    if (qc0 + 31 < prow0) continue;  // the whole 32 x 32 block has q < p
-                    if (P.nseg > 1) {
-                        // this segment's partial: (double) of its first chunk, then sequential f64 adds
-                        double* dst = part + (int64_t)(qc0 - q0) * BMP + (p - p0);
-                        if (c == c0) {
+                    if (qc0 + 31 < prow0 || prow0 >= n) continue;  // the whole block has q < p, or no row p < n
+                    if (split || qc0 == prow0) {
+                        // element by element, q >= p: the first chunk of a split partial is stored, every other
+                        // chunk added (all loads before any store).  A split partial is private to its CTA and
+                        // L2-resident while its segment runs; its bulk additions measured slower than this.
+                        if (split && c == c0) {
 #pragma unroll
-                            for (int i = 0; i < 32; i++) dst[i * BMP] = (double)v[i];
-                        } else {
-                            double old[32];
+                            for (int i = 0; i < 32; i++) {
+                                const int q = qc0 + i;
+                                if (p < n && q < n && q >= p) dst[(int64_t)(q - qofs) * ld + (p - pofs)] = (double)v[i];
+                            }
+                            continue;
+                        }
+                        double old[32];
 #pragma unroll
-                            for (int i = 0; i < 32; i++) old[i] = dst[i * BMP];
+                        for (int i = 0; i < 32; i++) {
+                            const int q = qc0 + i;
+                            old[i] = (p < n && q < n && q >= p) ? dst[(int64_t)(q - qofs) * ld + (p - pofs)] : 0.0;
+                        }
 #pragma unroll
-                            for (int i = 0; i < 32; i++) dst[i * BMP] = __dadd_rn(old[i], (double)v[i]);
+                        for (int i = 0; i < 32; i++) {
+                            const int q = qc0 + i;
+                            if (p < n && q < n && q >= p)
+                                dst[(int64_t)(q - qofs) * ld + (p - pofs)] = __dadd_rn(old[i], (double)v[i]);
                         }
                         continue;
                     }
-                    // H[q][p] += D[p][q] for q >= p (lanes along a row of H).  All 32 loads are issued before any
-                    // store, so the read-modify-writes overlap instead of waiting on each other.
-                    double old[32];
+                    const uint32_t bytes = (uint32_t)min(32, n - prow0) * 8u;  // n % 8 == 0: a multiple of 64
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int q = qc0 + i;
-                        old[i] = (p < n && q < n && q >= p) ? P.h[(int64_t)q * n + p] : 0.0;
-                    }
+                    for (int hb = 0; hb < 2; hb++) {
+                        if (lane == 0) bulk_wait_read_le1();  // this buffer's previous additions have read it
+                        __syncwarp();
+                        double* buf = ebuf + bi * (EPI_BUF_BYTES / 8);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int q = qc0 + i;
-                        if (p < n && q < n && q >= p) P.h[(int64_t)q * n + p] = __dadd_rn(old[i], (double)v[i]);
+                        for (int i = 0; i < 16; i++) buf[i * 32 + lane] = (double)v[hb * 16 + i];
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            for (int i = 0; i < 16; i++) {
+                                const int q = qc0 + hb * 16 + i;
+                                if (q < n)
+                                    bulk_add_f64(dst + (int64_t)(q - qofs) * ld + (prow0 - pofs),
+                                                 ebuf_s + (uint32_t)(bi * EPI_BUF_BYTES + i * 256), bytes);
+                            }
+                            bulk_commit();
+                        }
+                        bi ^= 1;
                     }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 mbar_arrive(&acce[b]);
             }
         }
+        if (lane == 0) bulk_wait_all();  // the additions are performed before the CTA leaves
     }
 
     // teardown: every role is done with the tensor memory
@@ -350,7 +402,7 @@ namespace syrk {
 __global__ void __launch_bounds__(128) syrk_reduce_kernel(const Params P) {
     const int tile = blockIdx.x;
     int pb, qb;
-    tile_coords(tile, P.tiles_q, pb, qb);
+    tile_coords(P, tile, pb, qb);
     const int pl = threadIdx.x, p = pb * BMP + pl, n = P.n;
     if (p >= n) return;
     for (int ql = blockIdx.y * 32; ql < blockIdx.y * 32 + 32; ql++) {
@@ -427,7 +479,18 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     P.tiles_p = (n + BMP - 1) / BMP;
     P.tiles_q = (n + BNQ - 1) / BNQ;
     P.ntiles = 0;
-    for (int pb = 0; pb < P.tiles_p; pb++) P.ntiles += P.tiles_q - (pb >> 1);
+    // Tiles (p block, q block) holding some q >= p, in bands of TILE_BAND p blocks; within a band q block by
+    // q block.  Consecutive tiles share the q block (B operand), and a wave of one tile per SM spans about
+    // TILE_BAND p blocks x (SMs / TILE_BAND) q blocks, so each token chunk of X that a wave reads is a small part
+    // of the n channels and stays in L2 for every tile of the wave that needs it.
+    std::vector<int2> order;
+    for (int b0 = 0; b0 < P.tiles_p; b0 += TILE_BAND) {
+        const int b1 = std::min(P.tiles_p, b0 + TILE_BAND);
+        for (int qb = b0 >> 1; qb < P.tiles_q; qb++)
+            for (int pb = b0; pb < b1; pb++)
+                if ((pb >> 1) <= qb) order.push_back(make_int2(pb, qb));
+    }
+    P.ntiles = (int)order.size();
     P.lower_only = lower_only ? 1 : 0;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -441,13 +504,19 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     P.cps = (nchunks + nseg - 1) / nseg;
     P.nseg = (nchunks + P.cps - 1) / P.cps;
     P.scratch = nullptr;
-    if (P.nseg > 1)
-        CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&P.scratch,
-                                       sizeof(double) * (size_t)P.nseg * P.ntiles * BMP * BNQ, st));
+    if (P.nseg > 1) {
+        const size_t sb = sizeof(double) * (size_t)P.nseg * P.ntiles * BMP * BNQ;
+        CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&P.scratch, sb, st));
+    }
+    // one allocation: the error flag, then the tile order
     int* err = nullptr;
-    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&err, sizeof(int), st));
+    const size_t tiles_off = 16;
+    CDCLQ_CUDA_TRY(cudaMallocAsync((void**)&err, tiles_off + order.size() * sizeof(int2), st));
     CDCLQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    int2* tiles_dev = reinterpret_cast<int2*>(reinterpret_cast<char*>(err) + tiles_off);
+    CDCLQ_CUDA_TRY(cudaMemcpyAsync(tiles_dev, order.data(), order.size() * sizeof(int2), cudaMemcpyHostToDevice, st));
     P.err = err;
+    P.tiles = tiles_dev;
     auto kern = syrk_bf16_kernel<NS>;
     const size_t smem = smem_bytes(NS);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

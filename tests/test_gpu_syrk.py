@@ -24,7 +24,9 @@ def exact_gram(x):
     return xf.T @ xf, np.abs(xf).T @ np.abs(xf)
 
 
-@pytest.mark.parametrize("t,n", [(5000, 192), (4096, 256), (2048, 136), (300, 64), (6000, 520)])
+# small n: fewer output tiles than SMs, tokens split into segments; n = 3080: a wave of tiles or more (no split),
+# ragged p and q tiles (3080 = 24 * 128 + 8) and a partial second chunk
+@pytest.mark.parametrize("t,n", [(5000, 192), (4096, 256), (2048, 136), (300, 64), (6000, 520), (2100, 3080)])
 def test_bf16_gram_matches_exact_within_f32_chunk_error(gpu, t, n):
     import torch
 
