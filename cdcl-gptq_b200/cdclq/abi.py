@@ -74,6 +74,7 @@ class CBatchLayer(ctypes.Structure):
         ("scales", ctypes.c_void_p),
         ("zeros", ctypes.c_void_p),
         ("stats", ctypes.POINTER(CLayerStats)),
+        ("colsq", ctypes.c_void_p),
     ]
 
 

@@ -67,6 +67,11 @@ class ModelBatch:
     the rows shard_rows() gives it, and `run` needs torch.distributed initialised (NCCL).  With w_sharded=True
     each W entry holds only this rank's rows (shard_rows(d_out, cfg.row_chunk, rank, world, rotate=layer index))
     and layers without rows on this rank may be None.
+
+    With a skeleton (cfg.skeleton_pct > 0) the column permutation ranks columns by H_jj * ||W_:j||^2 over ALL
+    rows of the layer (src/engine.rs:271-304); a row-sharded rank therefore computes those scores from the full
+    W (cdclq_column_scores_device, the same row-ordered f64 sums as a single-GPU run) and hands them to the
+    library, which needs the full W on every rank (w_sharded=False).
     """
 
     def __init__(self, torch, layers, inputs, H, W, cfg, rank=0, world=1, on_device=True, distribute_factors=True,
@@ -75,6 +80,10 @@ class ModelBatch:
         self.cfg = cfg
         self.rank, self.world = rank, world
         self.on_device = on_device
+        skel_scores = world > 1 and cfg.skeleton_pct > 0.0
+        if skel_scores and w_sharded:
+            raise ValueError("a skeleton ranks columns by the whole weight matrix: every rank needs the full W "
+                             "(w_sharded=False) to compute the column scores")
         self.keep = []
         self.ins = (CBatchInput * len(inputs))()
         for i, (_, n) in enumerate(inputs):
@@ -119,6 +128,8 @@ class ModelBatch:
             L.scales = o["scales"].data_ptr()
             L.zeros = o["zeros"].data_ptr()
             L.stats = ctypes.pointer(self.stats[i])
+            if skel_scores:
+                L.colsq = self._column_scores(w, H[inp], d_out, d_in)
             self.h2d_bytes += rs * d_in * 4
             self.d2h_bytes += rs * d_in + 2 * rs * ng * 4 + d_in * 4 + ng
         self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1) in rows)
@@ -136,6 +147,19 @@ class ModelBatch:
             self.which = ctypes.cast(self._which, ctypes.c_void_p)
             self.u_out = ctypes.cast(self._u_out, ctypes.c_void_p)
             self.u_in = ctypes.cast(self._u_in, ctypes.c_void_p)
+
+    def _column_scores(self, w, h, d_out, n):
+        """Skeleton column scores of the full W (device f64, or pinned host f64 when on_device=False)."""
+        torch = self.torch
+        wd = w if w.is_cuda else w.cuda()
+        hd = h if h.is_cuda else h.cuda()
+        cs = torch.empty(n, dtype=torch.float64, device="cuda")
+        check(lib().cdclq_column_scores_device(ctypes.c_void_p(wd.data_ptr()), d_out, n, ctypes.c_void_p(hd.data_ptr()),
+                                               ctypes.c_void_p(cs.data_ptr()), None))
+        if not self.on_device:
+            cs = cs.cpu().pin_memory()
+        self.keep.append(cs)
+        return cs.data_ptr()
 
     def run(self, stream_handle):
         c = self.cfg.to_c()

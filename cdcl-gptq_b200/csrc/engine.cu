@@ -238,6 +238,7 @@ struct LayerReq {
     float* zeros = nullptr;
     cdclq_layer_stats* stats = nullptr;
     uint32_t* chunk_passes = nullptr;  // host, optional
+    const double* colsq = nullptr;     // optional skeleton column scores over the full matrix (host or device)
 };
 
 static thread_local cdclq_run_profile g_profile;
@@ -546,14 +547,21 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
                 w_uploads.push_back(li);
         }
         if (skel) {
-            double* cs_dev = nullptr;
-            if ((rc = ar.alloc(&cs_dev, P.n))) return rc;
-            if ((rc = launch_colsq(P.w_dev, hdiag_dev[L.input], (int)P.d_out, (int)P.n, cs_dev, st))) return rc;
             std::vector<double> colsq(P.n);
-            CDCLQ_CUDA_TRY(cudaMemcpyAsync(colsq.data(), cs_dev, P.n * sizeof(double), cudaMemcpyDeviceToHost, st));
-            CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+            if (L.colsq && !on_device) {  // caller-supplied scores of the full matrix (a row shard's caller)
+                std::copy(L.colsq, L.colsq + P.n, colsq.begin());
+            } else if (L.colsq) {
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(colsq.data(), L.colsq, P.n * sizeof(double), cudaMemcpyDeviceToHost, st));
+                CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+            } else {
+                double* cs_dev = nullptr;
+                if ((rc = ar.alloc(&cs_dev, P.n))) return rc;
+                if ((rc = launch_colsq(P.w_dev, hdiag_dev[L.input], (int)P.d_out, (int)P.n, cs_dev, st))) return rc;
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(colsq.data(), cs_dev, P.n * sizeof(double), cudaMemcpyDeviceToHost, st));
+                CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+                ar.free_one(cs_dev);
+            }
             compute_perm(hdiag[L.input], &colsq, P.n, P.g, cfg, P.perm, P.nskel);
-            ar.free_one(cs_dev);
         } else {
             P.perm = input_perm[L.input];
             P.nskel = 0;
@@ -1242,6 +1250,7 @@ static int quantize_batch_impl(const cdclq_batch_input* inputs, size_t n_inputs,
         L.scales = layers[i].scales;
         L.zeros = layers[i].zeros;
         L.stats = layers[i].stats;
+        L.colsq = layers[i].colsq;
         if (L.input >= n_inputs) return set_error(CDCLQ_ERR_ARG, "layer input index out of range");
         size_t g = effective_group(*cfg, in[L.input].n);
         (g <= 1024 ? small : large).push_back(L);
@@ -1446,6 +1455,22 @@ int cdclq_gram_accumulate(const float* x, const float* y, size_t t, size_t n, do
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(hd, h, n * n * sizeof(double), cudaMemcpyHostToDevice, st));
     if ((rc = cdclq_gram_accumulate_device(xd, yd, t, n, hd, st))) return rc;
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(h, hd, n * n * sizeof(double), cudaMemcpyDeviceToHost, st));
+    CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+    return CDCLQ_OK;
+}
+
+int cdclq_column_scores_device(const float* w, size_t d_out, size_t n, const float* h, double* colsq_out,
+                               void* stream) {
+    if (!w || !h || !colsq_out || n == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
+    if (n > 0x7fffffff || d_out > 0x7fffffff) return set_error(CDCLQ_ERR_ARG, "matrix too large");
+    int rc = ensure_device();
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    Arena ar(st);
+    double* hdiag = nullptr;
+    if ((rc = ar.alloc(&hdiag, n))) return rc;
+    if ((rc = launch_hdiag(h, (int)n, hdiag, st))) return rc;
+    if ((rc = launch_colsq(w, hdiag, (int)d_out, (int)n, colsq_out, st))) return rc;
     CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
     return CDCLQ_OK;
 }

@@ -144,6 +144,11 @@ typedef struct cdclq_batch_layer {
     float* scales;    /* d_out * ng */
     float* zeros;     /* d_out * ng */
     cdclq_layer_stats* stats;
+    /* optional input, NULL = computed from this call's rows: the skeleton's column scores (n f64, original
+     * column order) over the layer's FULL weight matrix, as cdclq_column_scores_device returns them.  A caller
+     * that passes only a shard of the rows (several GPUs) and configures a skeleton must supply them, or the
+     * ranking of src/engine.rs:271-304 would see only its rows. */
+    const double* colsq;
 } cdclq_batch_layer;
 
 /* Quantize many layers in one batched pass: every layer's rows are in flight at once, so small layers
@@ -152,6 +157,12 @@ typedef struct cdclq_batch_layer {
  * 1: all are device pointers (stats stays a host pointer), `stream` is used for all work. */
 int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
                          size_t n_layers, const cdclq_config* cfg, int on_device, void* stream);
+
+/* The skeleton ranking's column scores (src/engine.rs:271-304, the ||W_:j||^2 of compute_perm): colsq[j] =
+ * sum over rows r = 0 .. d_out-1, in order, of (f64) w[r][j] squared (f64 multiply, then add); 0 where the raw
+ * H_jj == 0 (dead column).  w: d_out x n f32 original order, h: n x n f32, colsq_out: n f64; device pointers. */
+int cdclq_column_scores_device(const float* w, size_t d_out, size_t n, const float* h, double* colsq_out,
+                               void* stream);
 
 /* ---- ingest and packed output on the device (src/io.rs) ------------------------------------------------- */
 

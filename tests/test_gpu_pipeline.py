@@ -126,3 +126,33 @@ def test_rank_local_weight_shards_give_the_same_rows(gpu):
         assert_same(outputs(a), outputs(b))
     with pytest.raises(ValueError):
         ModelBatch(torch, layers, inputs, hs, ws, CFG, rank=0, world=2, distribute_factors=False, w_sharded=True)
+
+
+def test_skeleton_row_shards_use_the_full_matrix_ranking(gpu):
+    """A skeleton ranks columns by H_jj ||W_:j||^2 over all rows: row shards take the column scores of the full
+    W (cdclq_column_scores_device) and concatenate to the single-GPU result; the ranking from a shard's own rows
+    would differ."""
+    import torch
+
+    from cdclq.pipeline import ModelBatch
+
+    cfg = Config(group=32, block=64, sub_block=32, row_chunk=32, passes=3, skeleton_pct=30.0)
+    layers, inputs, hs, ws = model(torch, "cuda")
+    full = ModelBatch(torch, layers, inputs, hs, ws, cfg)
+    full.run(0)
+    torch.cuda.synchronize()
+    ref = outputs(full)
+    assert any(int(o["gbits"][0]) == cfg.skeleton_bits for o in ref)  # the skeleton is in use
+    world = 2
+    parts = []
+    for rank in range(world):
+        mb = ModelBatch(torch, layers, inputs, hs, ws, cfg, rank=rank, world=world, distribute_factors=False)
+        mb.run(0)
+        torch.cuda.synchronize()
+        parts.append(dict(zip(mb.names, zip(mb.shards, outputs(mb)))))
+    for li, (name, d_out, _, _) in enumerate(layers):
+        rows = sorted((p[name] for p in parts if name in p), key=lambda x: x[0][0])
+        for k in ("codes", "scales", "zeros"):
+            assert np.array_equal(np.concatenate([o[k] for _, o in rows]), ref[li][k]), (name, k)
+        for _, o in rows:
+            assert np.array_equal(o["perm"], ref[li]["perm"]) and np.array_equal(o["gbits"], ref[li]["gbits"])

@@ -5,7 +5,7 @@ import ctypes
 import os
 import socket
 
-
+import pytest
 from conftest import ROOT
 
 TINYLLAMA_INPUTS = [2048, 2048, 2048, 5632] * 22
@@ -148,3 +148,16 @@ def test_factor_exchange_two_ranks_gloo():
     res.sort()
     assert all(ok for _, ok, _ in res)
     assert res[0][2] == res[1][2]  # both ranks derived the same owners
+
+
+def test_skeleton_shards_need_the_full_weights():
+    """Row shards with a skeleton: the column ranking needs the whole W, so rank-local weight shards are refused
+    before anything is allocated."""
+    import torch
+
+    from cdclq.abi import Config
+    from cdclq.pipeline import ModelBatch
+
+    cfg = Config(group=32, row_chunk=32, skeleton_pct=30.0)
+    with pytest.raises(ValueError, match="whole weight matrix"):
+        ModelBatch(torch, [("l0", 64, 128, 0)], [("in0", 128)], [None], [None], cfg, rank=0, world=2, w_sharded=True)
