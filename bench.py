@@ -337,153 +337,316 @@ def run_syrk_bench(args, torch):
         torch.cuda.empty_cache()
 
 
-L7_HIDDEN, L7_INTER, L7_LAYERS = 4096, 11008, 32
-L7_BLOCK = [("q_proj", L7_HIDDEN, L7_HIDDEN, "attn"), ("k_proj", L7_HIDDEN, L7_HIDDEN, "attn"),
-            ("v_proj", L7_HIDDEN, L7_HIDDEN, "attn"), ("o_proj", L7_HIDDEN, L7_HIDDEN, "o"),
-            ("gate_proj", L7_INTER, L7_HIDDEN, "mlp"), ("up_proj", L7_INTER, L7_HIDDEN, "mlp"),
-            ("down_proj", L7_HIDDEN, L7_INTER, "down")]
-L7_INPUT_DIM = {"attn": L7_HIDDEN, "o": L7_HIDDEN, "mlp": L7_HIDDEN, "down": L7_INTER}
+# ---- model-level configurations beyond configs[1]: configs[2] (Gemma-2B-shaped, skeleton), configs[3]
+# (Llama-2-7B-shaped, the north star, Hessians accumulated on the GPU) and configs[4] (Llama-3-70B stress layers)
+
+MODEL_SPECS = {
+    # hidden, intermediate, q/o width, k/v rows, decoder layers, blocks per single-GPU batch
+    "llama2-7b": dict(config=3, hidden=4096, inter=11008, q_out=4096, kv=4096, layers=32, per_batch=16,
+                      tokens="gauss", hessians_timed=True, outliers=0.001, label="Llama-2-7B-shaped"),
+    "gemma2b": dict(config=2, hidden=2048, inter=16384, q_out=2048, kv=256, layers=18, per_batch=18,
+                    tokens="student3", hessians_timed=False, outliers=0.0, label="Gemma-2B-shaped"),
+}
 
 
-def run_llama2_7b(args, torch, rank, world):
-    """The north-star configuration end to end: a Llama-2-7B-shaped model (32 layers, 6.48e9
-    bf16-valued weights N(0, 0.02^2) with 0.1 % of input columns x10), every distinct input's Hessian accumulated
-    on the GPU by the tensor-core SYRK from 262144 seeded bf16 activations (configs[0] channel profile), then
-    CDCL quantization at `--bits` with group 64, --mse-grid, refine-frac 0.25, row chunk 128.
-
-    Timed (CUDA events, max over ranks): the Hessian accumulations and the quantization.  Not timed: generating
-    the synthetic activations and weights.  N > 1: the distinct inputs are assigned to ranks (longest processing
-    time on n^2); each owner accumulates its Hessians over all tokens and broadcasts them (f32, NCCL); the
-    quantization is cdclq.pipeline.ModelBatch (row shards, factorisations spread, U broadcast).  One GPU: the
-    layers go through the engine in two groups of sixteen blocks (memory)."""
-    import cdclq
-    from cdclq import linalg
+def model_config(name, args):
     from cdclq.abi import Config
-    from cdclq.pipeline import ModelBatch, assign_factorisations, shard_rows
 
-    cdclq.lib()
-    dev = "cuda"
-    cfg = Config(bits=args.bits, group=64, mse_grid=True, refine_frac=0.25, row_chunk=ROW_CHUNK)
-    st = torch.cuda.current_stream()
+    if name == "llama2-7b":  # configs[3]: 4-bit and 2-bit, group 64, --mse-grid, refine-frac 0.25
+        return Config(bits=args.bits, group=args.group or 64, mse_grid=True, refine_frac=0.25, row_chunk=ROW_CHUNK)
+    # 4-bit, group 128, skeleton-pct 2 (skeleton groups at 8 bits)
+    return Config(bits=4, group=128, skeleton_pct=2.0, row_chunk=ROW_CHUNK)
+
+
+def spec_layers(spec):
+    """(layers, inputs) of a decoder stack: q, k, v, o, gate, up, down per block; distinct inputs attn (q/k/v),
+    o, mlp (gate/up) and down."""
+    h, it, qo, kv = spec["hidden"], spec["inter"], spec["q_out"], spec["kv"]
+    block = [("q_proj", qo, h, "attn"), ("k_proj", kv, h, "attn"), ("v_proj", kv, h, "attn"), ("o_proj", h, qo, "o"),
+             ("gate_proj", it, h, "mlp"), ("up_proj", it, h, "mlp"), ("down_proj", h, it, "down")]
+    dims = {"attn": h, "o": qo, "mlp": h, "down": it}
     layers, inputs = [], []
-    for b in range(L7_LAYERS):
+    for b in range(spec["layers"]):
         idx = {}
         for kind in ("attn", "o", "mlp", "down"):
             idx[kind] = len(inputs)
-            inputs.append(("model.layers.%d.%s" % (b, kind), L7_INPUT_DIM[kind]))
-        for name, d_out, d_in, kind in L7_BLOCK:
+            inputs.append(("model.layers.%d.%s" % (b, kind), dims[kind]))
+        for name, d_out, d_in, kind in block:
             layers.append(("model.layers.%d.%s" % (b, name), d_out, d_in, idx[kind]))
-    total_weights = sum(l[1] * l[2] for l in layers)
+    return layers, inputs
 
-    def weight(i, d_out, n, rows=None):
-        g = torch.Generator(device=dev)
-        g.manual_seed(90000 + i)
-        w = torch.randn(d_out, n, generator=g, device=dev) * 0.02
+
+def synth_weight(torch, i, d_out, n, std, outliers, bf16, rows=None, seed0=90000):
+    """Seeded N(0, std^2) weights, `outliers` of the input columns x10, bf16-valued unless bf16=False; `rows`
+    keeps a row range only (generated whole, so every rank sees the same matrix)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed0 + i)
+    w = torch.randn(d_out, n, generator=g, device="cuda") * std
+    if outliers > 0.0:
         gc = torch.Generator(device="cpu")
-        gc.manual_seed(91000 + i)
-        cols = torch.randperm(n, generator=gc)[:max(1, n // 1000)].to(dev)
-        w[:, cols] *= 10.0
-        if rows is not None:
-            w = w[rows[0]:rows[1]]
-        return w.to(torch.bfloat16).float().contiguous()
+        gc.manual_seed(seed0 + 1000 + i)
+        w[:, torch.randperm(n, generator=gc)[:max(1, int(round(n * outliers)))].to("cuda")] *= 10.0
+    if rows is not None:
+        w = w[rows[0]:rows[1]]
+    return (w.to(torch.bfloat16).float() if bf16 else w).contiguous()
 
-    def tokens(i, n):
-        scale = channel_profile(n, 3000 + i, torch, dev)
-        g = torch.Generator(device=dev)
-        g.manual_seed(4000 + i)
-        return (torch.randn(TOKENS, n, generator=g, device=dev) * scale).to(torch.bfloat16).contiguous()
 
-    ev_ms = 0.0  # timed device work on this rank
-    phase_ms = {"hessians": 0.0, "hessian_broadcast": 0.0, "quantization": 0.0}
+def synth_tokens(torch, scale, seed, t, kind):
+    """t seeded bf16 activations over len(scale) channels scaled per channel; kind "gauss" or "student3"
+    (heavy-tailed: N(0,1) / sqrt(chi2_3 / 3), Student-t with 3 degrees of freedom)."""
+    n = scale.numel()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    x = torch.randn(t, n, generator=g, device="cuda")
+    if kind == "student3":
+        chi = torch.randn(t, n, 3, generator=g, device="cuda").pow_(2).sum(-1)
+        x.div_(chi.div_(3.0).sqrt_())
+        del chi
+    return (x * scale).to(torch.bfloat16).contiguous()
 
-    def timed(fn, phase):
-        nonlocal ev_ms
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
+
+def gpu_hessian(torch, i, n, t, kind, stream, chunk=32768):
+    """Untimed input Hessian: H = X^T X (f32, accumulated in f64) of synthetic tokens with the configs[0] channel
+    profile, by the tensor-core SYRK in token chunks of `chunk` (a multiple of the reference's 2048, so the
+    result is that of one call) to keep wide inputs small on the device."""
+    from cdclq import linalg
+
+    scale = channel_profile(n, 3000 + i, torch, "cuda")
+    h64 = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    for t0 in range(0, t, chunk):
+        x = synth_tokens(torch, scale, 4000 + 7919 * i + t0 // chunk, min(chunk, t - t0), kind)
+        linalg.gram_accumulate_bf16_device(x, h64, lower_only=t0 + chunk < t, stream=stream)
+        del x
+    return h64.float()
+
+
+class PhaseClock:
+    """Device time of timed steps on one stream (CUDA events around each step, synchronised), per phase."""
+
+    def __init__(self, torch, stream, phases):
+        self.torch, self.st = torch, stream
+        self.ms = {p: 0.0 for p in phases}
+
+    def __call__(self, fn, phase):
+        e0, e1 = self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True)
+        e0.record(self.st)
         out = fn()
-        e1.record(st)
-        torch.cuda.synchronize()
-        ev_ms += e0.elapsed_time(e1)
-        phase_ms[phase] += e0.elapsed_time(e1)
+        e1.record(self.st)
+        self.torch.cuda.synchronize()
+        self.ms[phase] += e0.elapsed_time(e1)
         return out
 
-    # ---- Hessians: owners accumulate, then every rank receives them
-    owner = assign_factorisations([n for (_, n) in inputs], world, power=2) if world > 1 else [0] * len(inputs)
-    if world > 1:
-        torch.distributed.barrier()
-    H = [None] * len(inputs)
-    for i, (_, n) in enumerate(inputs):
-        if owner[i] == rank:
-            x = tokens(i, n)
-            h64 = torch.zeros(n, n, dtype=torch.float64, device=dev)
-            timed(lambda: linalg.gram_accumulate_bf16_device(x, h64, lower_only=False, stream=st.cuda_stream),
-                  "hessians")
-            H[i] = timed(lambda: h64.float(), "hessians")
-            del x, h64
-        else:
-            H[i] = torch.empty(n, n, dtype=torch.float32, device=dev)
-    if world > 1:
-        import torch.distributed as dist
+    def total(self):
+        return sum(self.ms.values())
 
-        def bcast():
-            for i, h in enumerate(H):
-                dist.broadcast(h, src=owner[i])
-        timed(bcast, "hessian_broadcast")
+
+def max_over_ranks(torch, values, world, op="max"):
+    if world == 1:
+        return list(values)
+    t = torch.tensor(list(values), dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX if op == "max" else torch.distributed.ReduceOp.SUM)
+    return [float(v) for v in t]
+
+
+def run_model(args, torch, rank, world):
+    """configs[3] (`--model llama2-7b`, the north star) and configs[2] (`--model gemma2b`) end to end.
+
+    32 Llama-2-7B-shaped blocks, 6.48e9 bf16-valued weights N(0, 0.02^2) with 0.1 % of input columns
+    x10; every distinct input's Hessian accumulated on the GPU by the tensor-core SYRK from 262144 seeded bf16
+    activations (configs[0] channel profile) INSIDE the timed region; then `--bits` (4 or 2), group 64 (or
+    `--group`), --mse-grid, refine-frac 0.25.  N > 1: Hessian owners by longest processing time on n^2, each
+    broadcast (f32, NCCL); quantization by cdclq.pipeline.ModelBatch on rank-local row shards.
+    18 Gemma-2B-shaped blocks (k/v 256 rows, intermediate 16384), 1.98e9 weights; Hessians from
+    262144 Student-t(3) tokens are inputs (built by the SYRK, not timed); 4-bit, group 128, skeleton-pct 2.
+    N > 1: every rank holds the full W for the skeleton's column scores.
+    Timed: CUDA events, max over ranks.  Not timed: synthetic activations and weights."""
+    import cdclq
+    from cdclq import linalg
+    from cdclq.pipeline import ModelBatch, assign_factorisations, shard_rows
+
+    cdclq.lib()
+    spec = MODEL_SPECS[args.model]
+    cfg = model_config(args.model, args)
+    st = torch.cuda.current_stream()
+    layers, inputs = spec_layers(spec)
+    total_weights = sum(l[1] * l[2] for l in layers)
+    skel = cfg.skeleton_pct > 0.0
+    clock = PhaseClock(torch, st, ("hessians", "hessian_broadcast", "quantization"))
+
+    # ---- Hessians
+    H = [None] * len(inputs)
+    if spec["hessians_timed"]:
+        owner = assign_factorisations([n for (_, n) in inputs], world, power=2) if world > 1 else [0] * len(inputs)
+        if world > 1:
+            torch.distributed.barrier()
+        for i, (_, n) in enumerate(inputs):
+            if owner[i] != rank:
+                H[i] = torch.empty(n, n, dtype=torch.float32, device="cuda")
+                continue
+            x = synth_tokens(torch, channel_profile(n, 3000 + i, torch, "cuda"), 4000 + i, TOKENS, spec["tokens"])
+            h64 = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+            clock(lambda: linalg.gram_accumulate_bf16_device(x, h64, lower_only=False, stream=st.cuda_stream),
+                  "hessians")
+            H[i] = clock(lambda: h64.float(), "hessians")
+            del x, h64
+        if world > 1:
+            def bcast():
+                for i, h in enumerate(H):
+                    torch.distributed.broadcast(h, src=owner[i])
+            clock(bcast, "hessian_broadcast")
+    else:
+        for i, (_, n) in enumerate(inputs):
+            H[i] = gpu_hessian(torch, i, n, TOKENS, spec["tokens"], st.cuda_stream)
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
 
     # ---- quantization
     stats = []
     eng = {k: 0.0 for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair", "ms_final")}
 
-    def add_profile():
+    def quantize(part, W, **kw):
+        b = ModelBatch(torch, part, inputs, H, W, cfg, on_device=True, **kw)
+        if world > 1:
+            torch.distributed.barrier()
+        clock(lambda: b.run(st.cuda_stream), "quantization")
         prof = cdclq._lib.last_run_profile()
         for k in eng:
             eng[k] += prof[k]
+        stats.extend(b.stats)
 
+    wstd, outl = 0.02, spec["outliers"]
     if world > 1:
         W = []
         for i, (_, d_out, n, _) in enumerate(layers):
-            r = shard_rows(d_out, ROW_CHUNK, rank, world, rotate=i)
-            W.append(weight(i, d_out, n, r) if r[1] > r[0] else None)
-        torch.distributed.barrier()
-        b = ModelBatch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True, w_sharded=True)
-        timed(lambda: b.run(st.cuda_stream), "quantization")
-        add_profile()
-        stats = list(b.stats)
-        del W, b
+            if skel:  # the skeleton's column scores need every row
+                W.append(synth_weight(torch, i, d_out, n, wstd, outl, True))
+            else:
+                r = shard_rows(d_out, ROW_CHUNK, rank, world, rotate=i)
+                W.append(synth_weight(torch, i, d_out, n, wstd, outl, True, r) if r[1] > r[0] else None)
+        quantize(layers, W, rank=rank, world=world, w_sharded=not skel)
+        del W
     else:
-        per = 16 * len(L7_BLOCK)
+        per = spec["per_batch"] * 7
         for l0 in range(0, len(layers), per):
             part = layers[l0:l0 + per]
-            W = [weight(l0 + j, d_out, n) for j, (_, d_out, n, _) in enumerate(part)]
-            b = ModelBatch(torch, part, inputs, H, W, cfg, on_device=True)
-            timed(lambda: b.run(st.cuda_stream), "quantization")
-            add_profile()
-            stats += list(b.stats)
-            del W, b
+            W = [synth_weight(torch, l0 + j, d_out, n, wstd, outl, True) for j, (_, d_out, n, _) in enumerate(part)]
+            quantize(part, W)
+            del W
             torch.cuda.empty_cache()
-    ms = ev_ms
-    loss = [sum(s.loss_gptq for s in stats), sum(s.loss_final for s in stats)]
-    phases = [phase_ms[k] for k in ("hessians", "hessian_broadcast", "quantization")]
+    loss = max_over_ranks(torch, [sum(s.loss_gptq for s in stats), sum(s.loss_final for s in stats)], world, "sum")
+    names = ("hessians", "hessian_broadcast", "quantization")
+    t = max_over_ranks(torch, [clock.total()] + [clock.ms[k] for k in names], world)
+    if rank == 0:
+        c3 = spec["config"] == 3
+        print(json.dumps({
+            "metric": "seconds per model quantized incl. %sCDCL repair" % ("Hessian accumulation and " if c3 else ""),
+            "value": t[0] * 1e-3, "unit": "s", "higher_is_better": False, "n_gpus": world,
+            "weights_per_s": total_weights / (t[0] * 1e-3),
+            "target_s": 60.0 if c3 else None, "target_gpus": 8 if c3 else None,
+            "config": {"workload": "%s model (configs[%d]): %d layers, %d linear layers, %.3g weights, %d Hessians "
+                                   "from %d %s bf16 tokens each%s" % (
+                                       spec["label"], spec["config"], spec["layers"], len(layers), total_weights,
+                                       len(inputs), TOKENS, "Student-t(3)" if spec["tokens"] == "student3" else "Gaussian",
+                                       " accumulated on the GPU inside the timed region" if c3 else " (inputs)"),
+                       "bits": cfg.bits, "group": cfg.group, "mse_grid": bool(cfg.mse_grid),
+                       "refine_frac": cfg.refine_frac, "skeleton_pct": cfg.skeleton_pct, "row_chunk": ROW_CHUNK},
+            "timed": ("tensor-core Hessian accumulation + quantization" if c3 else "quantization") +
+                     " (synthetic activation and weight generation excluded)",
+            "engine_phases_ms_rank0": eng,
+            "phases_s_max_over_ranks": {k: v * 1e-3 for k, v in zip(names, t[1:])},
+            "loss_gptq": loss[0], "loss_final": loss[1], "data": "synthetic (seeded)",
+        }), flush=True)
+
+
+def fp64_gemm_peak_tflops(torch):
+    """cuBLAS DGEMM (8192^3, f64) measured in this run: the FP64 roofline of the factorisation kernels (FP64
+    CUDA-core and DMMA peaks are the same on B200; the driver's peaks file has no FP64 figure)."""
+    a = torch.randn(8192, 8192, dtype=torch.float64, device="cuda")
+    b = torch.randn(8192, 8192, dtype=torch.float64, device="cuda")
+    for _ in range(2):
+        torch.matmul(a, b)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        torch.matmul(a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 5
+    del a, b
+    return 2.0 * 8192 ** 3 / (ms * 1e-3) / 1e12
+
+
+def run_stress70b(args, torch, rank, world):
+    """Llama-3-70B-shaped stress layers, down_proj 8192 x 28672 and q_proj 8192 x 8192, f32 weights
+    N(0, 0.015^2), Hessians from 262144 Student-t(3) tokens (inputs, built by the SYRK, not timed); 3-bit,
+    group 128, block 256, passes 8.  Timed separately (rank 0): the damped f64 Cholesky + triangular inverse of
+    the 28672-wide Hessian (cdclq_prepare_factors on that input alone), against a cuBLAS DGEMM measured in the
+    same run.  Then the quantization of both layers (which factorises again inside), max over ranks."""
+    import ctypes
+
+    import cdclq
+    from cdclq.abi import CBatchInput, Config
+    from cdclq.pipeline import ModelBatch, shard_rows
+
+    cdclq.lib()
+    cfg = Config(bits=3, group=128, block=256, passes=8, row_chunk=ROW_CHUNK)
+    st = torch.cuda.current_stream()
+    inputs = [("model.layers.0.mlp.down_proj", 28672), ("model.layers.0.self_attn.q_proj", 8192)]
+    layers = [("model.layers.0.mlp.down_proj", 8192, 28672, 0), ("model.layers.0.self_attn.q_proj", 8192, 8192, 1)]
+    total_weights = sum(l[1] * l[2] for l in layers)
+    H = [gpu_hessian(torch, 200 + i, n, TOKENS, "student3", st.cuda_stream, chunk=8192) for i, (_, n) in
+         enumerate(inputs)]
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    clock = PhaseClock(torch, st, ("factorisation", "quantization"))
+    fact = None
+    if rank == 0:
+        peak64 = fp64_gemm_peak_tflops(torch)
+        ins = (CBatchInput * len(inputs))()
+        for i, (_, ni) in enumerate(inputs):
+            ins[i].h = H[i].data_ptr()
+            ins[i].n = ni
+        n = inputs[0][1]
+        u = torch.empty(n, n, dtype=torch.float32, device="cuda")
+        which = (ctypes.c_size_t * 1)(0)
+        u_out = (ctypes.c_void_p * 1)(u.data_ptr())
+        c = cfg.to_c()
+
+        def factorise():
+            cdclq._lib.check(cdclq.lib().cdclq_prepare_factors(
+                ins, len(inputs), ctypes.cast(which, ctypes.c_void_p), 1, ctypes.byref(c),
+                ctypes.cast(u_out, ctypes.c_void_p), 1, ctypes.c_void_p(st.cuda_stream)))
+        factorise()  # warm-up (allocator pool, first-launch costs)
+        clock.ms["factorisation"] = 0.0
+        clock(factorise, "factorisation")
+        flops = 2.0 * n ** 3 / 3.0  # Cholesky n^3/3 + triangular inverse n^3/3
+        ms = clock.ms["factorisation"]
+        fact = {"n": n, "s": ms * 1e-3, "flops": flops, "tflops": flops / (ms * 1e-3) / 1e12,
+                "fp64_peak_tflops": peak64, "frac": flops / (ms * 1e-3) / 1e12 / peak64,
+                "peak_source": "cuBLAS DGEMM 8192^3 measured in this run"}
+        del u
+        torch.cuda.empty_cache()
+    W = []
+    for i, (_, d_out, n, _) in enumerate(layers):
+        r = shard_rows(d_out, ROW_CHUNK, rank, world, rotate=i) if world > 1 else (0, d_out)
+        W.append(synth_weight(torch, i, d_out, n, 0.015, 0.0, False, r, seed0=95000) if r[1] > r[0] else None)
+    b = ModelBatch(torch, layers, inputs, H, W, cfg, rank=rank, world=world, on_device=True, w_sharded=True)
     if world > 1:
-        t = torch.tensor([ms] + phases, dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, phases = float(t[0]), [float(v) for v in t[1:]]
-        lt = torch.tensor(loss, dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(lt)
-        loss = [float(lt[0]), float(lt[1])]
+        torch.distributed.barrier()
+    clock(lambda: b.run(st.cuda_stream), "quantization")
+    prof = cdclq._lib.last_run_profile()
+    loss = max_over_ranks(torch, [sum(s.loss_gptq for s in b.stats), sum(s.loss_final for s in b.stats)], world, "sum")
+    t = max_over_ranks(torch, [clock.ms["quantization"]], world)[0]
     if rank == 0:
         print(json.dumps({
-            "metric": "seconds per model quantized incl. Hessian accumulation and CDCL repair (north-star config)",
-            "value": ms * 1e-3, "unit": "s", "higher_is_better": False, "n_gpus": world,
-            "weights_per_s": total_weights / (ms * 1e-3), "target_s": 60.0, "target_gpus": 8,
-            "config": {"workload": "Llama-2-7B-shaped model (configs[3]): 32 layers, 224 linear layers, %.3g weights, "
-                                   "128 Hessians accumulated on the GPU from 262144 bf16 tokens each" % total_weights,
-                       "bits": args.bits, "group": 64, "mse_grid": True, "refine_frac": 0.25, "row_chunk": ROW_CHUNK},
-            "timed": "tensor-core Hessian accumulation + quantization (activation and weight generation excluded)",
-            "engine_phases_ms_rank0": eng,
-            "phases_s_max_over_ranks": {"hessians": phases[0] * 1e-3, "hessian_broadcast": phases[1] * 1e-3,
-                                        "quantization": phases[2] * 1e-3},
+            "metric": "seconds to quantize the configs[4] stress layers (incl. CDCL repair)", "value": t * 1e-3,
+            "unit": "s", "higher_is_better": False, "n_gpus": world, "weights_per_s": total_weights / (t * 1e-3),
+            "config": {"workload": "Llama-3-70B-shaped stress layers (configs[4]): down_proj 8192x28672 + q_proj "
+                                   "8192x8192, f32 weights, Hessians from 262144 Student-t(3) tokens (inputs)",
+                       "bits": 3, "group": 128, "block": 256, "passes": 8, "row_chunk": ROW_CHUNK},
+            "factorisation_n28672_rank0": fact,
+            "engine_phases_ms_rank0": {k: prof[k] for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair",
+                                                             "ms_final")},
             "loss_gptq": loss[0], "loss_final": loss[1], "data": "synthetic (seeded)",
         }), flush=True)
 
@@ -508,9 +671,12 @@ def main():
     ap.add_argument("--kernel", default="model", choices=["model", "syrk"],
                     help="syrk: time the bf16 tensor-core Hessian accumulation alone (one JSON line per width)")
     ap.add_argument("--syrk-widths", default="2048,4096,5632,11008", help="--kernel syrk: channel counts n")
-    ap.add_argument("--model", default="tinyllama", choices=["tinyllama", "llama2-7b"],
-                    help="llama2-7b: the north-star configuration (configs[3]) end to end, one extra JSON line")
+    ap.add_argument("--model", default="tinyllama", choices=["tinyllama", "llama2-7b", "gemma2b", "llama3-70b-layers"],
+                    help="tinyllama: configs[1] (the driver's line); llama2-7b: configs[3], the north star, Hessians "
+                         "accumulated on the GPU inside the timed region; gemma2b: configs[2]; llama3-70b-layers: "
+                         "configs[4].  The last three print their own JSON line.")
     ap.add_argument("--bits", type=int, default=4, help="--model llama2-7b: code width (4 or 2)")
+    ap.add_argument("--group", type=int, default=0, help="--model llama2-7b: group width (default 64, configs[3])")
     ap.add_argument("--syrk-tokens", type=int, default=TOKENS, help="--kernel syrk: tokens per Hessian")
     args = ap.parse_args()
 
@@ -540,8 +706,8 @@ def main():
         if world > 1:
             torch.distributed.destroy_process_group()
         return
-    if args.model == "llama2-7b":
-        run_llama2_7b(args, torch, rank, world)
+    if args.model in ("llama2-7b", "gemma2b", "llama3-70b-layers"):
+        (run_stress70b if args.model == "llama3-70b-layers" else run_model)(args, torch, rank, world)
         if world > 1:
             torch.distributed.destroy_process_group()
         return
