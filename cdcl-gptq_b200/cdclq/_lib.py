@@ -47,6 +47,8 @@ SIGNATURES = {
     "cdclq_gram_accumulate": (I32, [P, P, SZ, SZ, P]),
     "cdclq_gram_accumulate_bf16_device": (I32, [P, SZ, SZ, P, I32, P]),
     "cdclq_column_scores_device": (I32, [P, SZ, SZ, P, P, P]),
+    "cdclq_prepare_layer_factors": (I32, [ctypes.POINTER(CBatchInput), SZ, ctypes.POINTER(CBatchLayer), SZ, P, SZ, CFG,
+                                          P, I32, P]),
     "cdclq_gram_accumulate_device": (I32, [P, P, SZ, SZ, P, P]),
     "cdclq_gram_accumulate_device_noalloc": (I32, [P, P, SZ, SZ, P, P]),
     "cdclq_proxy_loss": (I32, [P, P, SZ, SZ, P, P]),

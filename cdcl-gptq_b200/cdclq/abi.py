@@ -75,6 +75,7 @@ class CBatchLayer(ctypes.Structure):
         ("zeros", ctypes.c_void_p),
         ("stats", ctypes.POINTER(CLayerStats)),
         ("colsq", ctypes.c_void_p),
+        ("u", ctypes.c_void_p),
     ]
 
 

@@ -71,7 +71,9 @@ class ModelBatch:
     With a skeleton (cfg.skeleton_pct > 0) the column permutation ranks columns by H_jj * ||W_:j||^2 over ALL
     rows of the layer (src/engine.rs:271-304); a row-sharded rank therefore computes those scores from the full
     W (cdclq_column_scores_device, the same row-ordered f64 sums as a single-GPU run) and hands them to the
-    library, which needs the full W on every rank (w_sharded=False).
+    library, which needs the full W on every rank (w_sharded=False).  The permutation then differs from layer to
+    layer, so the factorisations are spread per layer (cdclq_prepare_layer_factors, owners by LPT on n^3) and
+    each layer's U is broadcast from its owner.
     """
 
     def __init__(self, torch, layers, inputs, H, W, cfg, rank=0, world=1, on_device=True, distribute_factors=True,
@@ -93,11 +95,14 @@ class ModelBatch:
         rc = cfg.row_chunk
         if rc <= 0 and world > 1:
             raise ValueError("multi-GPU row sharding needs a pinned row_chunk (row chunks must not move)")
+        colsq = [self._column_scores(w, H[inp], d_out, d_in) for ((_, d_out, d_in, inp), w) in zip(layers, W)] \
+            if skel_scores else [None] * len(layers)
         rows = []
         for li, ((name, d_out, d_in, inp), w) in enumerate(zip(layers, W)):
             r0, r1 = shard_rows(d_out, rc, rank, world, rotate=li) if world > 1 else (0, d_out)
             if r1 > r0:
-                rows.append((name, d_out, d_in, inp, w, r0, r1))
+                rows.append((name, d_out, d_in, inp, w, r0, r1, li))
+        self.layer_index = [r[7] for r in rows]
         self.names = [r[0] for r in rows]
         self.shards = [(r[5], r[6]) for r in rows]
         self.lys = (CBatchLayer * len(rows))()
@@ -106,7 +111,7 @@ class ModelBatch:
         self.h2d_bytes = sum(int(h.numel()) * 4 for h in H)
         self.d2h_bytes = 0
         dev = "cuda" if on_device else "cpu"
-        for i, (name, d_out, d_in, inp, w, r0, r1) in enumerate(rows):
+        for i, (name, d_out, d_in, inp, w, r0, r1, li) in enumerate(rows):
             ng = num_groups(cfg, d_in)
             rs = r1 - r0
             wv = w if w_sharded else w[r0:r1]
@@ -129,10 +134,29 @@ class ModelBatch:
             L.zeros = o["zeros"].data_ptr()
             L.stats = ctypes.pointer(self.stats[i])
             if skel_scores:
-                L.colsq = self._column_scores(w, H[inp], d_out, d_in)
+                L.colsq = colsq[li]
             self.h2d_bytes += rs * d_in * 4
             self.d2h_bytes += rs * d_in + 2 * rs * ng * 4 + d_in * 4 + ng
-        self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1) in rows)
+        self.weights = sum((r1 - r0) * d_in for (_, _, d_in, _, _, r0, r1, _) in rows)
+
+        # skeleton: a factor per layer (its own permutation), spread over the ranks by LPT on n^3
+        self.layer_factors = skel_scores and distribute_factors
+        if self.layer_factors:
+            self.all_lys = (CBatchLayer * len(layers))()  # every layer, full rows: what the factor depends on
+            for li, ((_, d_out, d_in, inp), w) in enumerate(zip(layers, W)):
+                A = self.all_lys[li]
+                A.w = w.data_ptr()
+                A.d_out = d_out
+                A.input = inp
+                A.colsq = colsq[li]
+            ns = [d_in for (_, _, d_in, _) in layers]
+            self.lowner = assign_factorisations(ns, world)
+            self.lu = [torch.empty(n, n, dtype=torch.float32, device="cuda") for n in ns]
+            self.lmine = [li for li in range(len(layers)) if self.lowner[li] == rank]
+            self._lwhich = (ctypes.c_size_t * max(1, len(self.lmine)))(*self.lmine)
+            self._lu_out = (ctypes.c_void_p * max(1, len(self.lmine)))(*[self.lu[li].data_ptr() for li in self.lmine])
+            for i, li in enumerate(self.layer_index):
+                self.lys[i].u = self.lu[li].data_ptr()
 
         # factorisations spread over the ranks: factor buffers for every input, owners by LPT on n^3
         self.distributed = world > 1 and distribute_factors and cfg.skeleton_pct <= 0.0
@@ -164,6 +188,15 @@ class ModelBatch:
     def run(self, stream_handle):
         c = self.cfg.to_c()
         dev = 1 if self.on_device else 0
+        if self.layer_factors:
+            check(lib().cdclq_prepare_layer_factors(self.ins, len(self.ins), self.all_lys, len(self.all_lys),
+                                                    ctypes.cast(self._lwhich, ctypes.c_void_p), len(self.lmine),
+                                                    ctypes.byref(c), ctypes.cast(self._lu_out, ctypes.c_void_p), dev,
+                                                    ctypes.c_void_p(stream_handle)))
+            exchange_factors(self.lu, self.lowner)
+            check(lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys), ctypes.byref(c), dev,
+                                             ctypes.c_void_p(stream_handle)))
+            return
         if not self.distributed:
             check(lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys), ctypes.byref(c), dev,
                                              ctypes.c_void_p(stream_handle)))

@@ -239,6 +239,7 @@ struct LayerReq {
     cdclq_layer_stats* stats = nullptr;
     uint32_t* chunk_passes = nullptr;  // host, optional
     const double* colsq = nullptr;     // optional skeleton column scores over the full matrix (host or device)
+    const float* u = nullptr;          // optional caller-supplied factor of this layer's (input, perm) (device)
 };
 
 static thread_local cdclq_run_profile g_profile;
@@ -592,9 +593,11 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             PrepEntry pe;
             pe.n = P.n;
             pe.perm = P.perm;
-            // a caller-supplied factor stands for the input's W-independent permutation only
-            pe.ext_u = u_ext && u_ext[layers[li].input] && P.nskel == 0 &&
-                       !(cfg.skeleton_pct > 0.0 && P.g < P.n);
+            // a caller-supplied factor: the layer's own (computed for its permutation), or the input's, which
+            // stands for the input's W-independent permutation only
+            pe.ext_u = layers[li].u != nullptr ||
+                       (u_ext && u_ext[layers[li].input] && P.nskel == 0 && !(cfg.skeleton_pct > 0.0 && P.g < P.n));
+            if (pe.ext_u) pe.u = const_cast<float*>(layers[li].u ? layers[li].u : u_ext[layers[li].input]);
             preps.push_back(pe);
             prep_input.push_back(layers[li].input);
             found = (int)preps.size() - 1;
@@ -610,8 +613,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     for (size_t k = 0; k < preps.size(); k++) {
         PrepEntry& pe = preps[k];
         size_t n = pe.n;
-        if (pe.ext_u) {
-            pe.u = const_cast<float*>(u_ext[prep_input[k]]);
+        if (pe.ext_u) {  // pe.u is the caller's
             if ((rc = ar.alloc(&pe.h32, n * n))) return rc;
             if ((rc = ar.alloc(&pe.perm_dev, n))) return rc;
         } else if (cache) {
@@ -1251,6 +1253,7 @@ static int quantize_batch_impl(const cdclq_batch_input* inputs, size_t n_inputs,
         L.zeros = layers[i].zeros;
         L.stats = layers[i].stats;
         L.colsq = layers[i].colsq;
+        L.u = layers[i].u;
         if (L.input >= n_inputs) return set_error(CDCLQ_ERR_ARG, "layer input index out of range");
         size_t g = effective_group(*cfg, in[L.input].n);
         (g <= 1024 ? small : large).push_back(L);
@@ -1342,6 +1345,101 @@ int cdclq_prepare_factors(const cdclq_batch_input* inputs, size_t n_inputs, cons
         groups.push_back(std::move(g));
     }
     // factorize_groups waits on the host for every factor stream: the factors are complete on return
+    rc = factorize_groups(groups, *cfg, st);
+    if (!rc) CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+    return rc;
+}
+
+int cdclq_prepare_layer_factors(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
+                                size_t n_layers, const size_t* which, size_t n_which, const cdclq_config* cfg,
+                                float* const* u_out, int on_device, void* stream) {
+    if (!cfg || (!inputs && n_inputs) || (!layers && n_layers) || (!which && n_which) || (!u_out && n_which))
+        return set_error(CDCLQ_ERR_ARG, "null argument");
+    int rc = ensure_device();
+    if (rc) return rc;
+    if (n_which == 0) return CDCLQ_OK;
+    cudaStream_t st = stream ? (cudaStream_t)stream : (on_device ? (cudaStream_t)0 : lib_stream());
+    Arena ar(st);
+    // per input: the raw diagonal (host and device) and the Hessian on the device
+    std::vector<std::vector<double>> hdiag(n_inputs);
+    std::vector<double*> hdiag_dev(n_inputs, nullptr);
+    std::vector<const float*> h_dev(n_inputs, nullptr);
+    std::vector<PrepEntry> preps(n_which);
+    std::map<size_t, std::vector<size_t>> by_n;
+    for (size_t k = 0; k < n_which; k++) {
+        const size_t li = which[k];
+        if (li >= n_layers) return set_error(CDCLQ_ERR_ARG, "layer index out of range");
+        const cdclq_batch_layer& L = layers[li];
+        const size_t i = L.input;
+        if (i >= n_inputs) return set_error(CDCLQ_ERR_ARG, "layer input index out of range");
+        const size_t n = inputs[i].n;
+        if (n == 0 || !inputs[i].h || !u_out[k]) return set_error(CDCLQ_ERR_ARG, "null argument");
+        if ((rc = validate(*cfg, n))) return rc;
+        if ((rc = check_tiling(*cfg, n))) return rc;
+        if (!h_dev[i]) {
+            if (on_device) {
+                h_dev[i] = inputs[i].h;
+            } else {
+                float* hd = nullptr;
+                if ((rc = ar.alloc(&hd, n * n))) return rc;
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(hd, inputs[i].h, n * n * sizeof(float), cudaMemcpyHostToDevice, st));
+                h_dev[i] = hd;
+            }
+            hdiag[i].resize(n);
+            if ((rc = ar.alloc(&hdiag_dev[i], n))) return rc;
+            if ((rc = launch_hdiag(h_dev[i], (int)n, hdiag_dev[i], st))) return rc;
+            CDCLQ_CUDA_TRY(cudaMemcpyAsync(hdiag[i].data(), hdiag_dev[i], n * sizeof(double), cudaMemcpyDeviceToHost, st));
+            CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+        }
+        // the permutation exactly as the batch call builds it (src/engine.rs:271-304)
+        const size_t g = effective_group(*cfg, n);
+        const bool skel = cfg->skeleton_pct > 0.0 && g < n;
+        std::vector<double> colsq;
+        if (skel) {
+            colsq.resize(n);
+            if (L.colsq && !on_device) {
+                std::copy(L.colsq, L.colsq + n, colsq.begin());
+            } else if (L.colsq) {
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(colsq.data(), L.colsq, n * sizeof(double), cudaMemcpyDeviceToHost, st));
+                CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+            } else {
+                if (!L.w || L.d_out == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
+                const float* wd = L.w;
+                float* wtmp = nullptr;
+                if (!on_device) {
+                    if ((rc = ar.alloc(&wtmp, L.d_out * n))) return rc;
+                    CDCLQ_CUDA_TRY(cudaMemcpyAsync(wtmp, L.w, L.d_out * n * sizeof(float), cudaMemcpyHostToDevice, st));
+                    wd = wtmp;
+                }
+                double* cs_dev = nullptr;
+                if ((rc = ar.alloc(&cs_dev, n))) return rc;
+                if ((rc = launch_colsq(wd, hdiag_dev[i], (int)L.d_out, (int)n, cs_dev, st))) return rc;
+                CDCLQ_CUDA_TRY(cudaMemcpyAsync(colsq.data(), cs_dev, n * sizeof(double), cudaMemcpyDeviceToHost, st));
+                CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
+                ar.free_one(cs_dev);
+                if (wtmp) ar.free_one(wtmp);
+            }
+        }
+        PrepEntry& pe = preps[k];
+        size_t nskel = 0;
+        compute_perm(hdiag[i], skel ? &colsq : nullptr, n, g, *cfg, pe.perm, nskel);
+        pe.n = n;
+        pe.u = u_out[k];
+        pe.h32 = nullptr;  // only U is wanted: the quantizing ranks rebuild the damped Hessian themselves
+        if ((rc = ar.alloc(&pe.perm_dev, n))) return rc;
+        CDCLQ_CUDA_TRY(cudaMemcpyAsync(pe.perm_dev, pe.perm.data(), n * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+        by_n[n].push_back(k);
+    }
+    std::vector<FactorGroup> groups;
+    for (auto it = by_n.rbegin(); it != by_n.rend(); ++it) {  // widest first
+        FactorGroup g;
+        g.n = it->first;
+        for (size_t k : it->second) {
+            g.hs.push_back(h_dev[layers[which[k]].input]);
+            g.es.push_back(&preps[k]);
+        }
+        groups.push_back(std::move(g));
+    }
     rc = factorize_groups(groups, *cfg, st);
     if (!rc) CDCLQ_CUDA_TRY(cudaStreamSynchronize(st));
     return rc;

@@ -149,6 +149,9 @@ typedef struct cdclq_batch_layer {
      * that passes only a shard of the rows (several GPUs) and configures a skeleton must supply them, or the
      * ranking of src/engine.rs:271-304 would see only its rows. */
     const double* colsq;
+    /* optional input, NULL = factorised in the call: the factor U (n x n f32, device) of this layer's (input,
+     * permutation) pair, as cdclq_prepare_layer_factors returns it (computed once on another rank). */
+    const float* u;
 } cdclq_batch_layer;
 
 /* Quantize many layers in one batched pass: every layer's rows are in flight at once, so small layers
@@ -157,6 +160,16 @@ typedef struct cdclq_batch_layer {
  * 1: all are device pointers (stats stays a host pointer), `stream` is used for all work. */
 int cdclq_quantize_batch(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
                          size_t n_layers, const cdclq_config* cfg, int on_device, void* stream);
+
+/* Per-layer factors for weight-dependent permutations (skeleton_pct > 0; also valid without a skeleton): for
+ * each k, the factor U of layers[which[k]]'s (input, permutation) pair into u_out[k] (n x n f32, device), the
+ * permutation computed exactly as cdclq_quantize_batch computes it - from the descriptor's colsq when given,
+ * else from its rows (w, d_out; device pointers when on_device).  Only w, d_out, input and colsq of the
+ * descriptors are read.  A rank factorises its share; the factors are exchanged and handed back to
+ * cdclq_quantize_batch in the descriptors' `u` field. */
+int cdclq_prepare_layer_factors(const cdclq_batch_input* inputs, size_t n_inputs, const cdclq_batch_layer* layers,
+                                size_t n_layers, const size_t* which, size_t n_which, const cdclq_config* cfg,
+                                float* const* u_out, int on_device, void* stream);
 
 /* The skeleton ranking's column scores (src/engine.rs:271-304, the ||W_:j||^2 of compute_perm): colsq[j] =
  * sum over rows r = 0 .. d_out-1, in order, of (f64) w[r][j] squared (f64 multiply, then add); 0 where the raw

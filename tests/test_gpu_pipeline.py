@@ -156,3 +156,42 @@ def test_skeleton_row_shards_use_the_full_matrix_ranking(gpu):
             assert np.array_equal(np.concatenate([o[k] for _, o in rows]), ref[li][k]), (name, k)
         for _, o in rows:
             assert np.array_equal(o["perm"], ref[li]["perm"]) and np.array_equal(o["gbits"], ref[li]["gbits"])
+
+
+def test_layer_factors_give_the_batch_result(gpu):
+    """Skeleton permutations are per layer: cdclq_prepare_layer_factors computes a layer's factor for its own
+    permutation, and a batch given those factors (descriptor field `u`) returns the single-call result bit for
+    bit; one layer is left to factorise inside the call."""
+    import torch
+
+    import cdclq
+    from cdclq.pipeline import ModelBatch
+
+    cfg = Config(group=32, block=64, sub_block=32, row_chunk=32, passes=3, skeleton_pct=30.0)
+    layers, inputs, hs, ws = model(torch, "cuda")
+    ref = ModelBatch(torch, layers, inputs, hs, ws, cfg)
+    ref.run(0)
+    torch.cuda.synchronize()
+    mb = ModelBatch(torch, layers, inputs, hs, ws, cfg)
+    us = [torch.full((NS[inp], NS[inp]), float("nan"), dtype=torch.float32, device="cuda") for (inp, _) in SPECS]
+    mine = [0, 1, 3, 4]  # layer 2 is factorised inside the batch call
+    which = (ctypes.c_size_t * len(mine))(*mine)
+    u_out = (ctypes.c_void_p * len(mine))(*[us[i].data_ptr() for i in mine])
+    c = cfg.to_c()
+    L = cdclq.lib()
+    cdclq._lib.check(L.cdclq_prepare_layer_factors(mb.ins, len(NS), mb.lys, len(mb.lys),
+                                                   ctypes.cast(which, ctypes.c_void_p), len(mine), ctypes.byref(c),
+                                                   ctypes.cast(u_out, ctypes.c_void_p), 1, None))
+    torch.cuda.synchronize()
+    for i in mine:  # strictly lower part exactly 0, positive diagonal (src/linalg.rs:498-503)
+        u = us[i].cpu().numpy()
+        assert np.all(np.tril(u, -1) == 0.0) and np.all(np.diag(u) > 0.0)
+    # layers 0 and 1 share an input but not a permutation: their factors differ
+    assert not torch.equal(us[0], us[1])
+    for i in mine:
+        mb.lys[i].u = us[i].data_ptr()
+    cdclq._lib.check(L.cdclq_quantize_batch(mb.ins, len(NS), mb.lys, len(mb.lys), ctypes.byref(c), 1, None))
+    torch.cuda.synchronize()
+    assert_same(outputs(mb), outputs(ref))
+    for s, r in zip(mb.stats, ref.stats):
+        assert s.loss_gptq == r.loss_gptq and s.loss_final == r.loss_final and s.code_updates == r.code_updates
