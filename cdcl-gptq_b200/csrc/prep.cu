@@ -269,25 +269,140 @@ __device__ __forceinline__ void dgemm_tile(double (&acc)[TM][4], FA fa, FB fb, i
     }
 }
 
-// Cholesky step 3 (src/linalg.rs:242-271): A22[i][c] -= sum_t P[i][t] P[c][t] for kend <= c <= i < n,
-// lower 64x64 tiles only (the reference also updates some upper-triangle garbage that is never read).
-// Zero-padded k beyond kb contributes exact zeros; each accumulator runs t = 0..kb-1 in order.
-__global__ void __launch_bounds__(256) chol_trail_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
-    __shared__ __align__(16) double smem[DTile<4>::SMEM_DOUBLES];
+// f64 GEMM tile core with paired fragments: CTA tile (32*RP) x 64 outputs, 256 threads as 16 (ty) x 16 (tx);
+// thread (ty, tx) owns the row pairs 2ty + 32i + {0, 1} (i < RP) and the column pairs 2tx + 32j + {0, 1}
+// (j < 2), so each k-step reads its fragments with 16-byte shared-memory loads: RP + 2 loads (RP + 4
+// wavefronts) per 8 RP DFMA, half the shared-memory traffic per DFMA of dgemm_tile, whose 4-row fragments
+// need a load per value.  Staging as in dgemm_tile (register prefetch of the next K stage, 16 at a time);
+// each accumulator receives its products in increasing k (the fixed order).  Dynamic shared memory:
+// DTile2<RP>::SMEM_BYTES.
+template <int RP>
+struct DTile2 {
+    static constexpr int ROWS = 32 * RP;
+    static constexpr int ALD = ROWS + 2;  // even: 16-byte aligned pairs
+    static constexpr int BLD = 64 + 2;
+    static constexpr int APER = ROWS * DKT / 256;
+    static constexpr int BPER = 64 * DKT / 256;
+    static constexpr int STAGE = DKT * ALD + DKT * BLD;  // doubles
+    static constexpr size_t SMEM_BYTES = 2 * (size_t)STAGE * sizeof(double);
+    static __device__ __forceinline__ int row(int ty, int i) { return 2 * ty + 32 * (i >> 1) + (i & 1); }
+    static __device__ __forceinline__ int col(int tx, int j) { return 2 * tx + 32 * (j >> 1) + (j & 1); }
+};
+
+template <int RP, bool B_ALONG_K, class FA, class FB>
+__device__ __forceinline__ void dgemm_tile2(double (&acc)[2 * RP][4], FA fa, FB fb, int kbeg, int kend,
+                                            double* smem) {
+    using T = DTile2<RP>;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    double ra[T::APER], rb[T::BPER];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int m = 0; m < T::APER; m++) {
+            int idx = tid + 256 * m, r = idx / DKT, k = k0 + (idx % DKT);
+            ra[m] = (k < kend) ? fa(r, k) : 0.0;
+        }
+#pragma unroll
+        for (int m = 0; m < T::BPER; m++) {
+            int idx = tid + 256 * m, c, k;
+            if (B_ALONG_K) {
+                c = idx / DKT;
+                k = k0 + (idx % DKT);
+            } else {
+                k = k0 + idx / 64;
+                c = idx % 64;
+            }
+            rb[m] = (k < kend) ? fb(k, c) : 0.0;
+        }
+    };
+    auto store = [&](int buf) {
+        double* As = smem + buf * T::STAGE;
+        double* Bs = As + DKT * T::ALD;
+#pragma unroll
+        for (int m = 0; m < T::APER; m++) {
+            int idx = tid + 256 * m, r = idx / DKT, kk = idx % DKT;
+            As[kk * T::ALD + r] = ra[m];
+        }
+#pragma unroll
+        for (int m = 0; m < T::BPER; m++) {
+            int idx = tid + 256 * m, c, kk;
+            if (B_ALONG_K) {
+                c = idx / DKT;
+                kk = idx % DKT;
+            } else {
+                kk = idx / 64;
+                c = idx % 64;
+            }
+            Bs[kk * T::BLD + c] = rb[m];
+        }
+    };
+    if (kbeg >= kend) return;
+    fetch(kbeg);
+    store(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += DKT) {
+        const bool more = k0 + DKT < kend;
+        if (more) fetch(k0 + DKT);
+        const double* A = smem + buf * T::STAGE;
+        const double* Bq = A + DKT * T::ALD;
+#pragma unroll
+        for (int kk = 0; kk < DKT; kk++) {
+            double av[2 * RP], bv[4];
+#pragma unroll
+            for (int i = 0; i < RP; i++) {
+                const double2 a = *reinterpret_cast<const double2*>(A + kk * T::ALD + 2 * ty + 32 * i);
+                av[2 * i] = a.x;
+                av[2 * i + 1] = a.y;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const double2 b = *reinterpret_cast<const double2*>(Bq + kk * T::BLD + 2 * tx + 32 * j);
+                bv[2 * j] = b.x;
+                bv[2 * j + 1] = b.y;
+            }
+#pragma unroll
+            for (int i = 0; i < 2 * RP; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fma_rn(av[i], bv[j], acc[i][j]);
+        }
+        if (more) store(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+}
+
+// Cholesky step 3 (src/linalg.rs:242-271): A22[i][c] -= sum_t P[i][t] P[c][t] for kend <= c <= i < n, in
+// tiles of 128 rows x 64 columns holding some c <= i (the reference also updates some upper-triangle garbage
+// that is never read).  Zero-padded k beyond kb contributes exact zeros; each accumulator runs t = 0..kb-1 in
+// order.  Tile index -> (row block ti, column tile tc): row block ti has min(T64, 2 ti + 2) column tiles.
+__host__ __device__ inline long long chol_trail_tiles(int rows) {
+    const long long t64 = (rows + 63) / 64, t128 = (rows + 127) / 128, b = t64 / 2;
+    return b * (b + 1) + (t128 - b) * t64;
+}
+
+__global__ void __launch_bounds__(256, 2) chol_trail_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    extern __shared__ __align__(16) double dsm[];
     const CholArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
     double* A = ar.a;
     const int kend = k + kb;
-    // tile index -> (ti, tc), tc <= ti
-    const long long x = blockIdx.x;
-    int ti = (int)((sqrt(8.0 * (double)x + 1.0) - 1.0) * 0.5);
-    while ((long long)(ti + 1) * (ti + 2) / 2 <= x) ti++;
-    while ((long long)ti * (ti + 1) / 2 > x) ti--;
-    const int tc = (int)(x - (long long)ti * (ti + 1) / 2);
-    const int r0 = kend + ti * 64, c0 = kend + tc * 64;
-    double acc[4][4];
+    const int t64 = (n - kend + 63) / 64, b = t64 / 2;
+    const long long x = blockIdx.x, cb = (long long)b * (b + 1);
+    int ti, tc;
+    if (x < cb) {  // row blocks ti < b: 2 ti + 2 column tiles each, ti (ti + 1) tiles before ti
+        ti = (int)((sqrt(4.0 * (double)x + 1.0) - 1.0) * 0.5);
+        while ((long long)(ti + 1) * (ti + 2) <= x) ti++;
+        while ((long long)ti * (ti + 1) > x) ti--;
+        tc = (int)(x - (long long)ti * (ti + 1));
+    } else {
+        ti = b + (int)((x - cb) / t64);
+        tc = (int)((x - cb) % t64);
+    }
+    const int r0 = kend + ti * 128, c0 = kend + tc * 64;
+    using T = DTile2<4>;
+    double acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
     auto fa = [&](int r, int t) -> double {
@@ -298,24 +413,25 @@ __global__ void __launch_bounds__(256) chol_trail_kernel(const CholArgs* __restr
         int cc = c0 + c;
         return (cc < n) ? A[(int64_t)cc * n + k + t] : 0.0;
     };
-    dgemm_tile<4, true>(acc, fa, fb, 0, kb, smem);
+    dgemm_tile2<4, true>(acc, fa, fb, 0, kb, dsm);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 #pragma unroll
-    for (int a = 0; a < 4; a++) {
-        int i = r0 + ty + 16 * a;
+    for (int a = 0; a < 8; a++) {
+        int i = r0 + T::row(ty, a);
         if (i >= n) continue;
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            int c = c0 + tx + 16 * b;
+        for (int bb = 0; bb < 4; bb++) {
+            int c = c0 + T::col(tx, bb);
             if (c <= i) {
                 double* p = A + (int64_t)i * n + c;
-                *p = __dsub_rn(*p, acc[a][b]);
+                *p = __dsub_rn(*p, acc[a][bb]);
             }
         }
     }
 }
 
 static int run_cholesky(const CholArgs* args_dev, int nitems, int n, cudaStream_t st) {
+    cudaFuncSetAttribute(chol_trail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DTile2<4>::SMEM_BYTES);
     for (int k = 0; k < n; k += NB) {
         int kb = min(NB, n - k);
         int kend = k + kb;
@@ -326,9 +442,8 @@ static int run_cholesky(const CholArgs* args_dev, int nitems, int n, cudaStream_
             cudaFuncSetAttribute(chol_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
             dim3 gp((rows_below + 127) / 128, nitems);
             CDCLQ_LAUNCH(chol_panel_kernel, gp, 128, smem2, st, args_dev, n, k, kb);
-            long long T = (rows_below + 63) / 64;
-            dim3 gt((unsigned)(T * (T + 1) / 2), nitems);
-            CDCLQ_LAUNCH(chol_trail_kernel, gt, 256, 0, st, args_dev, n, k, kb);
+            dim3 gt((unsigned)chol_trail_tiles(rows_below), nitems);
+            CDCLQ_LAUNCH(chol_trail_kernel, gt, 256, DTile2<4>::SMEM_BYTES, st, args_dev, n, k, kb);
         }
     }
     cudaError_t e = cudaGetLastError();
@@ -379,9 +494,11 @@ __global__ void __launch_bounds__(128) tri_diag_kernel(const TriArgs* __restrict
 
 // Triangular inverse step 2 (src/linalg.rs:307-325): T[i][j] = sum_k L[s+i][k] Y[k][j], k in [0, s).
 // Y is lower triangular: for the column tile starting at j0 every k < j0 multiplies an exact zero, so the
-// accumulation starts at k = j0.  One CTA covers all w <= 96 rows of the block and 64 columns.
-__global__ void __launch_bounds__(256) tri_gemm1_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
-    __shared__ __align__(16) double smem[DTile<6>::SMEM_DOUBLES];
+// accumulation starts at k = j0.  One CTA covers all w <= 96 rows of the block and 64 columns (the j0 = 0
+// tile's chain of s terms sets a step's duration when one matrix is factorised alone; splitting the rows over
+// three 32-row CTAs measured slower, the smaller tile costing more than the shorter chain saved).
+__global__ void __launch_bounds__(256, 2) tri_gemm1_kernel(const TriArgs* __restrict__ args, int n, int s, int w) {
+    extern __shared__ __align__(16) double dsm[];
     const TriArgs ar = args[blockIdx.y];
     if (ar.status->err) return;
     const int j0 = blockIdx.x * 64;
@@ -397,15 +514,15 @@ __global__ void __launch_bounds__(256) tri_gemm1_kernel(const TriArgs* __restric
         int j = j0 + c;
         return (j < s) ? Y[(int64_t)k * n + j] : 0.0;
     };
-    dgemm_tile<6, false>(acc, fa, fb, j0, s, smem);
+    dgemm_tile2<3, false>(acc, fa, fb, j0, s, dsm);
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 #pragma unroll
     for (int a = 0; a < 6; a++) {
-        int i = ty + 16 * a;
+        int i = DTile2<3>::row(ty, a);
         if (i >= w) continue;
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-            int j = j0 + tx + 16 * b;
+            int j = j0 + DTile2<3>::col(tx, b);
             if (j < s) ar.t[(int64_t)i * n + j] = acc[a][b];
         }
     }
@@ -454,7 +571,7 @@ static int run_tri_inverse(const TriArgs* args_dev, int nitems, int n, cudaStrea
         CDCLQ_LAUNCH(tri_diag_kernel, nitems, 128, smem, st, args_dev, n, s, w);
         if (s > 0) {
             dim3 g((s + 63) / 64, nitems);
-            CDCLQ_LAUNCH(tri_gemm1_kernel, g, 256, 0, st, args_dev, n, s, w);
+            CDCLQ_LAUNCH(tri_gemm1_kernel, g, 256, DTile2<3>::SMEM_BYTES, st, args_dev, n, s, w);
             CDCLQ_LAUNCH(tri_gemm2_kernel, g, 256, 0, st, args_dev, n, s, w);
         }
     }

@@ -14,7 +14,7 @@ def spd(n, seed):
     return m @ m.T + np.eye(n)
 
 
-@pytest.mark.parametrize("n", [1, 7, 96, 97, 150, 300])
+@pytest.mark.parametrize("n", [1, 7, 96, 97, 150, 300, 700])
 def test_cholesky_bit_exact(gpu, n):
     from cdclq import linalg
 
@@ -26,7 +26,7 @@ def test_cholesky_bit_exact(gpu, n):
     assert np.array_equal(np.tril(a), np.tril(b))
 
 
-@pytest.mark.parametrize("n", [5, 96, 200, 385])
+@pytest.mark.parametrize("n", [5, 96, 200, 385, 700])
 def test_tri_inverse_bit_exact(gpu, n):
     from cdclq import linalg
 
@@ -37,7 +37,7 @@ def test_tri_inverse_bit_exact(gpu, n):
     assert np.array_equal(y1, y2)
 
 
-@pytest.mark.parametrize("n", [10, 200, 333])
+@pytest.mark.parametrize("n", [10, 200, 333, 700])
 def test_upper_chol_of_inverse_bit_exact_and_contract(gpu, n):
     """src/linalg.rs:471-504 contract plus bit-exactness against the oracle."""
     from cdclq import linalg
