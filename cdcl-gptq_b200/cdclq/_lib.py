@@ -46,6 +46,7 @@ SIGNATURES = {
     "cdclq_upper_chol_of_inverse": (I32, [P, SZ, P]),
     "cdclq_gram_accumulate": (I32, [P, P, SZ, SZ, P]),
     "cdclq_gram_accumulate_bf16_device": (I32, [P, SZ, SZ, P, I32, P]),
+    "cdclq_gram_accumulate_half_device": (I32, [P, I32, SZ, SZ, P, I32, P]),
     "cdclq_column_scores_device": (I32, [P, SZ, SZ, P, P, P]),
     "cdclq_prepare_layer_factors": (I32, [ctypes.POINTER(CBatchInput), SZ, ctypes.POINTER(CBatchLayer), SZ, P, SZ, CFG,
                                           P, I32, P]),

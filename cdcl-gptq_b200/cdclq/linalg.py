@@ -42,6 +42,33 @@ def gram_accumulate(x, y, t, n, h):
     return h
 
 
+def gram_accumulate_device(x, h, stream=0):
+    """H (f64, device tensor, in place) += X^T X for X a (t, n) f32 device tensor: the bit-exact f32 path
+    (src/linalg.rs:388-418: token chunks of 2048, f32 sums in increasing token order, widened into H), both
+    triangles."""
+    t, n = int(x.shape[0]), int(x.shape[1])
+    assert h.shape == (n, n) and h.is_contiguous() and x.is_contiguous()
+    check(lib().cdclq_gram_accumulate_device(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(x.data_ptr()), t, n,
+                                             ctypes.c_void_p(h.data_ptr()), ctypes.c_void_p(stream)))
+    return h
+
+
+def gram_accumulate_half_device(x, h, lower_only=False, stream=0):
+    """H (f64, device tensor, in place) += X^T X for X a (t, n) bf16 or f16 device tensor on the tcgen05 tensor
+    cores (token chunks of 2048 accumulated in f32, then widened into H; src/linalg.rs:392-416)."""
+    import torch
+
+    t, n = int(x.shape[0]), int(x.shape[1])
+    assert h.shape == (n, n) and h.is_contiguous() and x.is_contiguous()
+    code = {torch.bfloat16: 2, torch.float16: 1}.get(x.dtype)
+    if code is None:
+        raise TypeError("half Gram: x must be bf16 or f16, got %s" % x.dtype)
+    check(lib().cdclq_gram_accumulate_half_device(ctypes.c_void_p(x.data_ptr()), code, t, n,
+                                                  ctypes.c_void_p(h.data_ptr()), 1 if lower_only else 0,
+                                                  ctypes.c_void_p(stream)))
+    return h
+
+
 def gram_accumulate_bf16_device(x_bf16, h, lower_only=False, stream=0):
     """H (f64, device tensor, in place) += X^T X for X a (t, n) bf16 device tensor, on the tcgen05 tensor cores:
     the token chunks of 2048 of src/linalg.rs:392 are accumulated in f32 inside the tensor core, then widened

@@ -1578,7 +1578,17 @@ int cdclq_gram_accumulate_bf16_device(const void* x_bf16, size_t t, size_t n, do
     if (!x_bf16 || !h || n == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
     int rc = ensure_device();  // the split-token partials come from the (caching) stream-ordered pool
     if (rc) return rc;
-    return launch_gram_bf16_tc(x_bf16, (int64_t)t, (int)n, h, lower_only, (cudaStream_t)stream);
+    return launch_gram_half_tc(x_bf16, true, (int64_t)t, (int)n, h, lower_only, (cudaStream_t)stream);
+}
+
+int cdclq_gram_accumulate_half_device(const void* x, int dtype, size_t t, size_t n, double* h, int lower_only,
+                                      void* stream) {
+    if (!x || !h || n == 0) return set_error(CDCLQ_ERR_ARG, "null argument");
+    if (dtype != CDCLQ_DTYPE_BF16 && dtype != CDCLQ_DTYPE_F16)
+        return set_error(CDCLQ_ERR_ARG, "half Gram: dtype must be CDCLQ_DTYPE_BF16 or CDCLQ_DTYPE_F16");
+    int rc = ensure_device();
+    if (rc) return rc;
+    return launch_gram_half_tc(x, dtype == CDCLQ_DTYPE_BF16, (int64_t)t, (int)n, h, lower_only, (cudaStream_t)stream);
 }
 
 int cdclq_proxy_loss(const float* w_t, const float* w_hat, size_t rows, size_t n, const float* h, double* out) {

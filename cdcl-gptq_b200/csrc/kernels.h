@@ -140,7 +140,8 @@ int launch_sgemm(int m, int n, int k, float alpha, const float* a, int64_t lda, 
                  int64_t ldb, bool b_trans, float beta, float* c, int64_t ldc, cudaStream_t st);
 // Gram accumulation h += x^T y (f32 products, chunks of 2048 tokens widened into f64)
 int launch_gram_f32(const float* x, const float* y, int64_t t, int n, double* h, float* tmp, cudaStream_t st);
-int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_only, cudaStream_t st);
+// bf16 (bf16 = true) or f16 activations; both kinds are exact products in f32.
+int launch_gram_half_tc(const void* x, bool bf16, int64_t t, int n, double* h, int lower_only, cudaStream_t st);
 
 // Elementwise helpers (gemm.cu)
 int launch_sub(const float* a, const float* b, int64_t count, float* out, cudaStream_t st);

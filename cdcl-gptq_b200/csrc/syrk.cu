@@ -119,14 +119,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return d;
 }
 
-// Instruction descriptor: D f32, A and B bf16, both MN-major, M = 128, N = 256.
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | ((uint32_t)(BNQ >> 3) << 17) |
-                           ((uint32_t)(BMP >> 4) << 24);
+// Instruction descriptor: D f32, A and B both bf16 (BF16) or both f16, both MN-major, M = 128, N = 256.
+template <bool BF16>
+__host__ __device__ constexpr uint32_t idesc() {
+    return (1u << 4) | ((BF16 ? 1u : 0u) << 7) | ((BF16 ? 1u : 0u) << 10) | (1u << 15) | (1u << 16) |
+           ((uint32_t)(BNQ >> 3) << 17) | ((uint32_t)(BMP >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+template <bool BF16>
+__device__ __forceinline__ void mma_half(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc<BF16>()), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -178,7 +182,7 @@ __device__ __forceinline__ void tile_coords(const Params& P, int tile, int& pb, 
     qb = t.y;
 }
 
-template <int NSTAGES>
+template <int NSTAGES, bool BF16>
 __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_constant__ CUtensorMap tmap, const Params P) {
     constexpr int NS = NSTAGES;  // shared-memory stages
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(THREADS, 1) syrk_bf16_kernel(const __grid_cons
                         const uint32_t sa = a_base + s * STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
                         for (int k = 0; k < KB / 16; k++)
-                            mma_bf16(d, smem_desc(sa + k * 2048, BOX_BYTES, 1024), smem_desc(sb + k * 2048, BOX_BYTES, 1024),
+                            mma_half<BF16>(d, smem_desc(sa + k * 2048, BOX_BYTES, 1024), smem_desc(sb + k * 2048, BOX_BYTES, 1024),
                                      (kb | k) != 0 ? 1u : 0u);
                         mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
                     }
@@ -455,23 +459,23 @@ static EncodeTiledFn encode_tiled_fn() {
     return fn;
 }
 
-int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_only, cudaStream_t st) {
+int launch_gram_half_tc(const void* x, bool bf16, int64_t t, int n, double* h, int lower_only, cudaStream_t st) {
     using namespace syrk;
     if (t <= 0) return 0;
-    if (n % 8 != 0) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: n must be a multiple of 8 (16-byte rows)");
-    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: x must be 16-byte aligned");
-    if (t > 0x7fffffffLL - CHUNK) return set_error(CDCLQ_ERR_ARG, "bf16 Gram: too many tokens for one call");
+    if (n % 8 != 0) return set_error(CDCLQ_ERR_ARG, "half Gram: n must be a multiple of 8 (16-byte rows)");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return set_error(CDCLQ_ERR_ARG, "half Gram: x must be 16-byte aligned");
+    if (t > 0x7fffffffLL - CHUNK) return set_error(CDCLQ_ERR_ARG, "half Gram: too many tokens for one call");
     EncodeTiledFn enc = encode_tiled_fn();
-    if (!enc) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: cuTensorMapEncodeTiled is unavailable");
+    if (!enc) return set_error(CDCLQ_ERR_CUDA, "half Gram: cuTensorMapEncodeTiled is unavailable");
     CUtensorMap map;
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)t};
     cuuint64_t strides[1] = {(cuuint64_t)n * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)KB};
     cuuint32_t estr[2] = {1, 1};
-    CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+    CUresult cr = enc(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: tensor map encoding failed");
+    if (cr != CUDA_SUCCESS) return set_error(CDCLQ_ERR_CUDA, "half Gram: tensor map encoding failed");
     Params P;
     P.h = h;
     P.n = n;
@@ -517,7 +521,7 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(tiles_dev, order.data(), order.size() * sizeof(int2), cudaMemcpyHostToDevice, st));
     P.err = err;
     P.tiles = tiles_dev;
-    auto kern = syrk_bf16_kernel<NS>;
+    auto kern = bf16 ? syrk_bf16_kernel<NS, true> : syrk_bf16_kernel<NS, false>;
     const size_t smem = smem_bytes(NS);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
@@ -545,7 +549,7 @@ int launch_gram_bf16_tc(const void* x, int64_t t, int n, double* h, int lower_on
     cudaFreeAsync(err, st);
     if (P.scratch) cudaFreeAsync(P.scratch, st);
     if (e != cudaSuccess) return cuda_error(e, "syrk_bf16_kernel");
-    if (herr) return set_error(CDCLQ_ERR_CUDA, "bf16 Gram: a pipeline wait timed out (kernel abandoned its tiles)");
+    if (herr) return set_error(CDCLQ_ERR_CUDA, "half Gram: a pipeline wait timed out (kernel abandoned its tiles)");
     return 0;
 }
 

@@ -231,6 +231,10 @@ int cdclq_gram_accumulate(const float* x, const float* y, size_t t, size_t n, do
  * as src/linalg.rs:392-416 does.  Only the lower triangle of h is written when lower_only != 0. */
 int cdclq_gram_accumulate_bf16_device(const void* x_bf16, size_t t, size_t n, double* h, int lower_only,
                                       void* stream);
+/* The same for f16 or bf16 activations (dtype CDCLQ_DTYPE_F16 / CDCLQ_DTYPE_BF16; f16 x f16 products are exact
+ * in f32 as well): what a half-precision model's forward pass hands to the Hessian capture. */
+int cdclq_gram_accumulate_half_device(const void* x, int dtype, size_t t, size_t n, double* h, int lower_only,
+                                      void* stream);
 /* Device variant of gram_accumulate for f32 activations (bit-exact with the f32 path above). */
 int cdclq_gram_accumulate_device(const float* x, const float* y, size_t t, size_t n, double* h, void* stream);
 /* No counterpart in the reference.  Same computation and result as cdclq_gram_accumulate_device, but the

@@ -119,3 +119,23 @@ def test_bf16_gram_downstream_codes(gpu):
     same = float(np.mean(qa.codes == qb.codes)) if np.array_equal(qa.perm, qb.perm) else 0.0
     print("identical codes with the tensor-core Hessian: %.5f" % same)
     assert same >= 0.99
+
+
+def test_f16_gram_matches_exact_within_f32_chunk_error(gpu):
+    """f16 activations (what a half-precision model's forward pass produces) through the same tensor-core SYRK:
+    f16 x f16 products are exact in f32 too."""
+    import torch
+
+    from cdclq import linalg
+
+    t, n = 4500, 328
+    x = (bf16_tokens(torch, t, n, 4711).float() * 0.5).to(torch.float16)
+    xf = x.float().numpy().astype(np.float64)
+    ex, ab = xf.T @ xf, np.abs(xf).T @ np.abs(xf)
+    h = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_half_device(x.cuda(), h)
+    torch.cuda.synchronize()
+    got = h.cpu().numpy()
+    bound = ((t + 2047) // 2048) * 2048 * 2.0 ** -24 * ab + 1e-12
+    assert np.all(np.abs(got - ex) <= bound)
+    assert np.array_equal(got, got.T)
