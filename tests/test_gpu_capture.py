@@ -126,7 +126,7 @@ def test_captured_hessian_quantizes(gpu):
     g = torch.Generator().manual_seed(5)
     cap = capture(m, [torch.randint(0, 256, (2, 128), generator=g) for _ in range(4)])[0]
     name = "model.layers.0.mlp.down_proj"
-    w = m.get_submodule(name).weight.float().cpu().numpy()
+    w = m.get_submodule(name).weight.detach().float().cpu().numpy()
     h = cap.hessian(name).cpu().numpy()
     q, st = cdclq.quantize_layer(w, w.shape[0], w.shape[1], h, None, name, Config(bits=3, group=32, row_chunk=32))
     assert st.loss_final <= st.loss_gptq and np.all(q.codes <= 7)
