@@ -85,56 +85,54 @@ struct CholArgs {
     FactorStatus* status;
 };
 
-// One thread per row of the 96-row block (rows past kb are identity padding and never stored); the row lives
-// in registers.  Per column j: the owner of row j takes the square root of its diagonal (after every earlier
-// term was subtracted) and checks the pivot; rows below divide their column-j entry and publish it; then each
-// row subtracts its a[i][j] * a[c][j] terms for j < c <= i.  Two barriers per column.
-__global__ void __launch_bounds__(128) chol_diag_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
-    __shared__ double colj[2][NB];
-    __shared__ double dsh;
+// The block lives in shared memory (row stride NB + 1: the column reads of a warp fall in distinct banks); per
+// column j one thread takes the square root of the diagonal (after every earlier term was subtracted) and
+// checks the pivot, the rows below divide their column-j entry, then a 16 x 16 thread grid applies the
+// column's `- a[i][j]*a[c][j]` term to every (i, c) with j < c <= i (mul then sub, as the reference's scalar
+// code).  Three barriers per column and no work outside the triangle.
+constexpr int CHOL_LD = NB + 1;
+constexpr size_t CHOL_DIAG_SMEM = (size_t)NB * CHOL_LD * sizeof(double);
+
+__global__ void __launch_bounds__(256) chol_diag_kernel(const CholArgs* __restrict__ args, int n, int k, int kb) {
+    extern __shared__ double blk[];  // [NB][CHOL_LD], lower triangle of the diagonal block
     __shared__ int bad;
     const CholArgs ar = args[blockIdx.x];
     if (ar.status->err) return;
     double* A = ar.a;
-    const int i = threadIdx.x;  // block row (threads >= NB idle through the loop)
-    double x[NB];
-#pragma unroll
-    for (int c = 0; c < NB; c++)
-        x[c] = (i < kb && c <= i) ? A[(int64_t)(k + i) * n + (k + c)] : ((c == i) ? 1.0 : 0.0);
-    if (i == 0) bad = 0;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    for (int idx = tid; idx < kb * kb; idx += blockDim.x) {
+        const int i = idx / kb, c = idx - i * kb;
+        if (c <= i) blk[i * CHOL_LD + c] = A[(int64_t)(k + i) * n + (k + c)];
+    }
+    if (tid == 0) bad = 0;
     __syncthreads();
-#pragma unroll
-    for (int j = 0; j < NB; j++) {
-        if (i == j) {
-            double d = x[j];
-            if (j < kb && (!(d > 0.0) || !isfinite(d))) {
+    for (int j = 0; j < kb; j++) {
+        if (tid == 0) {
+            const double d = blk[j * CHOL_LD + j];
+            if (!(d > 0.0) || !isfinite(d)) {
                 bad = 1;
                 ar.status->err = 1;
                 ar.status->pivot = k + j;
                 ar.status->value = d;
             } else {
-                d = __dsqrt_rn(d);
-                x[j] = d;
-                dsh = d;
+                blk[j * CHOL_LD + j] = __dsqrt_rn(d);
             }
         }
         __syncthreads();
         if (bad) return;
-        if (i > j && i < NB) {
-            x[j] = __ddiv_rn(x[j], dsh);
-            colj[j & 1][i] = x[j];
+        const double dj = blk[j * CHOL_LD + j];
+        for (int i = j + 1 + tid; i < kb; i += blockDim.x) blk[i * CHOL_LD + j] = __ddiv_rn(blk[i * CHOL_LD + j], dj);
+        __syncthreads();
+        for (int i = j + 1 + ty; i < kb; i += 16) {
+            const double aij = blk[i * CHOL_LD + j];
+            for (int c = j + 1 + tx; c <= i; c += 16)
+                blk[i * CHOL_LD + c] = __dsub_rn(blk[i * CHOL_LD + c], __dmul_rn(aij, blk[c * CHOL_LD + j]));
         }
         __syncthreads();
-        if (i > j && i < NB) {
-#pragma unroll
-            for (int c = 0; c < NB; c++)  // constant trip count: unrolls into registers once j is known
-                if (c > j && c <= i) x[c] = __dsub_rn(x[c], __dmul_rn(x[j], colj[j & 1][c]));
-        }
     }
-    if (i < kb) {
-#pragma unroll
-        for (int c = 0; c < NB; c++)
-            if (c <= i) A[(int64_t)(k + i) * n + (k + c)] = x[c];
+    for (int idx = tid; idx < kb * kb; idx += blockDim.x) {
+        const int i = idx / kb, c = idx - i * kb;
+        if (c <= i) A[(int64_t)(k + i) * n + (k + c)] = blk[i * CHOL_LD + c];
     }
 }
 
@@ -432,10 +430,11 @@ __global__ void __launch_bounds__(256, 2) chol_trail_kernel(const CholArgs* __re
 
 static int run_cholesky(const CholArgs* args_dev, int nitems, int n, cudaStream_t st) {
     cudaFuncSetAttribute(chol_trail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DTile2<4>::SMEM_BYTES);
+    cudaFuncSetAttribute(chol_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CHOL_DIAG_SMEM);
     for (int k = 0; k < n; k += NB) {
         int kb = min(NB, n - k);
         int kend = k + kb;
-        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 128, 0, st, args_dev, n, k, kb);
+        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 256, CHOL_DIAG_SMEM, st, args_dev, n, k, kb);
         if (kend < n) {
             int rows_below = n - kend;
             size_t smem2 = (size_t)NB * NB * sizeof(double);
