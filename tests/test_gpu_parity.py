@@ -258,3 +258,32 @@ def test_batch_split_heavy_and_light_chunks(gpu):
         assert stats[i].loss_gptq == sb.loss_gptq
         assert abs(stats[i].loss_final - sb.loss_final) <= 1e-9 * sb.loss_final
         assert stats[i].code_updates == sb.code_updates
+
+
+def configs0_problem(seed=2024):
+    """configs[0] of the north star, seeded: W 2048 x 2048 f32 N(0, 0.02^2) with 1 % of input columns x8; X 16384
+    tokens x 2048 channels, Gaussian with log-normal channel scales (sigma 1), 0.5 % of channels x20 and 1 % dead;
+    H = X^T X accumulated in f64, handed over as f32."""
+    n, t = 2048, 16384
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, n)) * 0.02).astype(np.float32)
+    w[:, rng.permutation(n)[:n // 100]] *= 8.0
+    scale = np.exp(rng.standard_normal(n))
+    p = rng.permutation(n)
+    scale[p[:round(0.005 * n)]] *= 20.0
+    scale[p[round(0.005 * n):round(0.005 * n) + round(0.01 * n)]] = 0.0
+    h = np.zeros((n, n))
+    for t0 in range(0, t, 4096):
+        x = rng.standard_normal((4096, n)) * scale
+        h += x.T @ x
+    return w, h.astype(np.float32)
+
+
+def test_parity_configs0_single_layer(gpu):
+    """configs[0] at full size (the reference's CPU-runnable case): 3-bit g128, block 128, sub-block 32, damp
+    0.01, act-order, passes 4, tol 1e-6, refine-frac 1, one sweep, refit on; row chunk pinned to 128."""
+    w, h = configs0_problem()
+    cfg = Config(bits=3, group=128, block=128, sub_block=32, damp=0.01, act_order=True, passes=4, tol=1e-6,
+                 refine_frac=1.0, cd_sweeps=1, row_chunk=128)
+    st = check_parity(w, h, cfg, 2048, 2048, what="configs[0]")
+    assert st.skeleton_groups == 0 and st.loss_final < st.loss_gptq
