@@ -234,7 +234,7 @@ def main(argv=None):
     if args.max_hessian_mem <= 0:
         sys.exit("--max-hessian-mem must be a positive number of GiB")
     tok = AutoTokenizer.from_pretrained(args.model)
-    model = AutoModelForCausalLM.from_pretrained(args.model, torch_dtype=getattr(torch, args.dtype))
+    model = AutoModelForCausalLM.from_pretrained(args.model, dtype=getattr(torch, args.dtype))
     model = model.to("cuda").eval()
     ids = tok(open(args.text, encoding="utf-8").read(), return_tensors="pt").input_ids[0]
     need = args.nsamples * args.seqlen

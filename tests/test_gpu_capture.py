@@ -130,3 +130,63 @@ def test_captured_hessian_quantizes(gpu):
     h = cap.hessian(name).cpu().numpy()
     q, st = cdclq.quantize_layer(w, w.shape[0], w.shape[1], h, None, name, Config(bits=3, group=32, row_chunk=32))
     assert st.loss_final <= st.loss_gptq and np.all(q.codes <= 7)
+
+
+def model_dir(torch, path):
+    """A tiny random Llama with a word-level tokenizer saved as a Hugging Face directory (built offline)."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    vocab = {"<unk>": 0}
+    for i in range(255):
+        vocab["w%d" % i] = i + 1
+    tk = Tokenizer(models.WordLevel(vocab=vocab, unk_token="<unk>"))
+    tk.pre_tokenizer = pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tk, unk_token="<unk>").save_pretrained(str(path))
+    tiny_llama(torch).save_pretrained(str(path))
+    return str(path)
+
+
+def test_command_line_writes_the_reference_files(gpu, tmp_path):
+    """`python -m cdclq.capture` (the reference script's arguments): one file, or one per pass under a small
+    --max-hessian-mem, each readable by HessianStore and equal to the library call on the same batches; with
+    --struct-chars the Hessians change."""
+    import torch
+    from transformers import AutoModelForCausalLM, AutoTokenizer
+
+    from cdclq import capture as cap
+    from cdclq.io import HessianStore
+
+    d = model_dir(torch, tmp_path / "model")
+    rng = np.random.default_rng(1)
+    text = tmp_path / "calib.txt"
+    text.write_text(" ".join("w%d" % v for v in rng.integers(0, 255, 600)))
+    args = ["--model", d, "--text", str(text), "--nsamples", "4", "--seqlen", "64", "--batch", "2", "--dtype",
+            "bfloat16"]
+    out = str(tmp_path / "h.safetensors")
+    cap.main(args + ["--out", out])
+    store = HessianStore([out])
+    assert set(store.index) == {"model.layers.%d.%s" % (b, m) for b in range(2)
+                                for m in ("self_attn.q_proj", "self_attn.o_proj", "mlp.gate_proj", "mlp.down_proj")}
+    assert store.resolve("model.layers.0.self_attn.k_proj") == "model.layers.0.self_attn.q_proj"
+    # the same capture through the library
+    tok = AutoTokenizer.from_pretrained(d)
+    m = AutoModelForCausalLM.from_pretrained(d, dtype=torch.bfloat16).cuda().eval()
+    ids = tok(text.read_text(), return_tensors="pt").input_ids[0][:4 * 64].view(4, 64)
+    lib = cap.capture(m, [ids[0:2], ids[2:4]])[0]
+    for owner in store.index:
+        h, _ = store.get_h(owner)
+        assert torch.equal(h, lib.h[owner]), owner
+    # several passes, several files
+    split = str(tmp_path / "s.safetensors")
+    cap.main(args + ["--out", split, "--max-hessian-mem", str(2.5 * 128 * 128 * 8 / 2 ** 30)])
+    files = sorted(str(p) for p in tmp_path.glob("s.*of*.safetensors"))
+    assert len(files) >= 2
+    multi = HessianStore(files)
+    for owner in store.index:
+        assert torch.equal(multi.get_h(owner)[0], store.get_h(owner)[0]), owner
+    # structural tokens weighted
+    wout = str(tmp_path / "w.safetensors")
+    cap.main(args + ["--out", wout, "--struct-chars", "7", "--struct-weight", "3.0"])
+    hw, _ = HessianStore([wout]).get_h("model.layers.0.mlp.gate_proj")
+    assert not torch.equal(hw, store.get_h("model.layers.0.mlp.gate_proj")[0])
