@@ -9,7 +9,6 @@ next, and that a width above the scratch's capacity is refused.  The file is nam
 """
 import ctypes
 
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
