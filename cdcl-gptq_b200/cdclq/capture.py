@@ -236,7 +236,8 @@ def main(argv=None):
     tok = AutoTokenizer.from_pretrained(args.model)
     model = AutoModelForCausalLM.from_pretrained(args.model, dtype=getattr(torch, args.dtype))
     model = model.to("cuda").eval()
-    ids = tok(open(args.text, encoding="utf-8").read(), return_tensors="pt").input_ids[0]
+    with open(args.text, encoding="utf-8") as f:
+        ids = tok(f.read(), return_tensors="pt").input_ids[0]
     need = args.nsamples * args.seqlen
     if ids.numel() < need:
         sys.exit("calibration text has %d tokens, need %d: use a bigger file or lower --nsamples/--seqlen"
