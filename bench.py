@@ -210,50 +210,124 @@ def load_peaks():
 
 
 # ------------------------------------------------------------------------------------------------------------
-def cpu_sample(layers, inputs, H, W, cfg):
-    """Time the CPU oracle on a bounded sample and extrapolate to the whole model (stated in `sample`).
+def host_cores():
+    """Host CPU threads this process may run on (the affinity mask, not OMP_NUM_THREADS: torchrun sets that
+    to 1 for every rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    Sample: the factorisation of one 2048-wide and one 5632-wide input, and one 128-row chunk of q_proj
-    (d_in 2048) and of down_proj (d_in 5632).  Model time = 22 x [sum over the block's 4 inputs of the
-    factorisation time of that width + sum over the block's 7 layers of (chunk time of that width) x (row
-    chunks of the layer) / cores], i.e. perfect scaling of row chunks over the host cores.
-    """
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as orc
 
-    cores = orc.max_threads()
-    t_prep, t_chunk = {}, {}
-    by_width = {}
-    for (name, d_out, d_in, inp) in layers[:7]:
-        by_width.setdefault(d_in, (name, d_out, d_in, inp))
-    t0 = time.time()
-    for d_in, (name, d_out, _, inp) in by_width.items():
-        li = [l[0] for l in layers].index(name)
-        h = H[inp].cpu().numpy()
-        w = W[li][:ROW_CHUNK].cpu().numpy()
-        ql, st = orc.quantize_layer(w, w.shape[0], d_in, h, None, inputs[inp][0], cfg)
-        t_prep[d_in] = st.secs_prepare
-        t_chunk[d_in] = st.secs_quant
-    wall = time.time() - t0
-    per_block = 0.0
-    for kind, n in INPUT_DIM.items():
-        per_block += t_prep[n]
-    for name, d_out, d_in, kind in BLOCK:
-        chunks = (d_out + ROW_CHUNK - 1) // ROW_CHUNK
-        per_block += t_chunk[d_in] * chunks / cores
-    model_s = N_LAYERS * per_block
-    weights = N_LAYERS * sum(d_out * d_in for (_, d_out, d_in, _) in BLOCK)  # the whole model, as model_s
+def reference_jobs(layers):
+    """The decoder layer's linear layers in the reference's job order (src/pipeline.rs:109-112: sorted by the
+    Hessian owner, then by layer name), so that the single-entry prep cache hits for q/k/v and gate/up."""
+    first = {}
+    for (name, _, _, inp) in layers:
+        first.setdefault(inp, name)  # the owner of an input is its first layer (q_proj, gate_proj)
+    return sorted(range(len(layers)), key=lambda i: (first[layers[i][3]], layers[i][0]))
+
+
+class CpuReference:
+    """The reference's CPU path (the oracle, oracle/: the C++ restatement, OpenMP over row chunks like the
+    reference's rayon) on one decoder layer of the model, one linear layer per step.
+
+    Step k quantizes job k mod 7 of the decoder layer in the reference's order, through the oracle's
+    quantize_layer with a single-entry prep cache keyed by the Hessian owner - exactly the reference's
+    sequential per-layer loop (src/pipeline.rs:121-175): the factorisation runs when the owner changes, q/k/v
+    and gate/up reuse it.  Seven consecutive steps are one whole decoder layer; the model time is 22 times the
+    decoder layer (the 22 layers are identical in shape), which is an extrapolation and is labelled as one."""
+
+    def __init__(self, layers, inputs, H, W, cfg, cores):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as orc
+
+        self.orc = orc
+        orc.set_threads(cores)
+        self.cores = cores
+        self.cfg = cfg
+        self.layers, self.inputs = layers, inputs
+        self.H = [h.float().cpu().numpy() for h in H]
+        self.W = [w.float().cpu().numpy() for w in W]
+        self.order = reference_jobs(layers)
+        self.cache = orc.PrepCache()
+        self.k = 0
+        self.results = {}
+
+    def step(self):
+        """One linear layer; returns (layer index, seconds, weights)."""
+        li = self.order[self.k % len(self.order)]
+        self.k += 1
+        name, d_out, d_in, inp = self.layers[li]
+        t0 = time.perf_counter()
+        ql, st = self.orc.quantize_layer(self.W[li], d_out, d_in, self.H[inp], None, self.inputs[inp][0], self.cfg,
+                                         self.cache)
+        dt = time.perf_counter() - t0
+        self.results[li] = (ql, st)
+        return li, dt, d_out * d_in
+
+    def decoder_layer_seconds(self, per_layer):
+        """Seconds of one decoder layer from per-layer timings {layer index: [seconds...]} (mean per layer)."""
+        return sum(statistics.mean(per_layer[li]) for li in self.order)
+
+
+def cpu_baseline_sample(layers, inputs, H, W, cfg):
+    """cpu_baseline (rank 0, N = 1): the CPU reference path over one whole decoder layer (7 steps of
+    CpuReference), timed; the model time is 22 decoder layers (stated as an extrapolation).  Also returns the
+    oracle's outputs for the parity check against the GPU's rows of the same layers."""
+    ref = CpuReference(layers, inputs, H, W, cfg, host_cores())
+    per, t0 = {}, time.perf_counter()
+    for _ in range(len(layers)):
+        li, dt, _ = ref.step()
+        per.setdefault(li, []).append(dt)
+    wall = time.perf_counter() - t0
+    layer_s = ref.decoder_layer_seconds(per)
+    model_s = N_LAYERS * layer_s
+    weights = N_LAYERS * sum(l[1] * l[2] for l in layers)
     return {
-        "value": weights / model_s, "unit": "weights/s", "cores": cores, "kind": "port",
-        "seconds_per_model": model_s, "sample_wall_s": wall,
-        "sample": ("CPU oracle (C++ restatement of the reference rayon path, OpenMP, %d threads): factorisation of "
-                   "one 2048- and one 5632-wide Hessian + one 128-row chunk of q_proj and down_proj, extrapolated "
-                   "to 22 decoder layers with row chunks spread over %d cores" % (cores, cores)),
-    }
+        "value": weights / model_s, "unit": "weights/s", "cores": ref.cores, "kind": "port",
+        "seconds_per_model": model_s, "seconds_per_decoder_layer": layer_s, "sample_wall_s": wall,
+        "sample": ("one whole decoder layer (7 linear layers, 4 factorisations, all row chunks) through the CPU "
+                   "oracle (C++ restatement of the reference's rayon path, OpenMP over row chunks, %d threads), "
+                   "timed; model = 22 x the decoder layer (extrapolation: identical layer shapes)" % ref.cores),
+    }, ref.results
+
+
+def parity_report(ref_results, batch, layers):
+    """The GPU's outputs for the decoder layer the CPU reference quantized (rows the persistent repair kernel
+    produced inside the timed model run) against the oracle's: fractions of identical codes, scales and zero
+    points, identical permutations, and the largest relative loss difference over the layers."""
+    n_codes = same_codes = n_groups = same_scales = same_zeros = 0
+    perms_identical = True
+    lg = lf = 0.0
+    for li, (ql, st) in sorted(ref_results.items()):
+        bi = batch.layer_index.index(li)
+        o = batch.outs[bi]
+        codes = o["codes"].cpu().numpy()
+        scales = o["scales"].cpu().numpy()
+        zeros = o["zeros"].cpu().numpy()
+        perms_identical &= bool(np.array_equal(o["perm"], ql.perm))
+        n_codes += codes.size
+        same_codes += int(np.count_nonzero(codes == ql.codes))
+        n_groups += scales.size
+        same_scales += int(np.count_nonzero(scales == ql.scales))
+        same_zeros += int(np.count_nonzero(zeros == ql.zeros))
+        s = batch.stats[bi]
+        lg = max(lg, abs(s.loss_gptq - st.loss_gptq) / st.loss_gptq)
+        lf = max(lf, abs(s.loss_final - st.loss_final) / st.loss_final)
+    return {"layers": [layers[li][0] for li in sorted(ref_results)], "weights": n_codes,
+            "codes_identical_frac": same_codes / n_codes, "scales_identical_frac": same_scales / n_groups,
+            "zeros_identical_frac": same_zeros / n_groups, "perms_identical": perms_identical,
+            "loss_gptq_rel_max": lg, "loss_final_rel_max": lf,
+            "bar": "north star: codes >= 99.99 % identical, ties only; losses within 1e-6 relative"}
 
 
 def run_reference_arm(args, torch, rank, world):
-    """`--impl reference`: the reference's CPU path (oracle port: Rust toolchain absent) on the host cores."""
+    """`--impl reference`: the reference's CPU path (the oracle port: no Rust toolchain on this image) on the
+    host cores, rank 0 only.  A step is one linear layer of configs[1]'s decoder layer in the reference's job
+    order (CpuReference): 7 consecutive steps are one decoder layer, each step timed as it runs.  value = model
+    weights / (22 x the decoder layer's time composed from the per-layer means of the timed steps); with fewer
+    than 7 timed steps, weights / seconds of the steps that ran."""
     if rank != 0:
         return
     cfg = bench_config()
@@ -261,26 +335,42 @@ def run_reference_arm(args, torch, rank, world):
     layers, inputs = model_layers(1)
     H = [make_hessian(n, 1000 + i, TOKENS, torch, device) for i, (_, n) in enumerate(inputs)]
     W = [make_weight(d_out, d_in, 50000 + i, torch, device) for i, (_, d_out, d_in, _) in enumerate(layers)]
+    ref = CpuReference(layers, inputs, H, W, cfg, host_cores())
+    for _ in range(args.warmup):
+        ref.step()
+    per, secs, wts = {}, [], 0
+    for _ in range(args.steps):
+        li, dt, nw = ref.step()
+        per.setdefault(li, []).append(dt)
+        secs.append(dt)
+        wts += nw
+    ms_per_step = 1e3 * sum(secs) / len(secs)
     full_layers, _ = model_layers(N_LAYERS)
-    vals = []
-    res = None
-    for i in range(args.warmup + args.steps):
-        res = cpu_sample(layers, inputs, H, W, cfg)
-        if i >= args.warmup:
-            vals.append(res["seconds_per_model"])
-    sec = statistics.median(vals)
-    weights = sum(l[1] * l[2] for l in full_layers)
-    value = weights / sec
+    model_weights = sum(l[1] * l[2] for l in full_layers)
+    if len(per) == len(layers):
+        layer_s = ref.decoder_layer_seconds(per)
+        model_s = N_LAYERS * layer_s
+        value = model_weights / model_s
+        how = ("per-layer mean times of the timed steps summed over the decoder layer's 7 linear layers, x22 "
+               "decoder layers (extrapolation: identical shapes)")
+    else:
+        value = wts / sum(secs)
+        model_s = model_weights / value
+        how = "weights / seconds of the timed steps (fewer than 7: not every layer of the decoder layer timed)"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "weights/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "seconds_per_model": sec,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "seconds_per_model": model_s,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(cfg),
-        "cpu_baseline": {"value": value, "unit": "weights/s", "cores": res["cores"], "kind": "port",
-                         "sample": res["sample"]},
+        "step": "one linear layer of the decoder layer, in the reference's job order (7 steps = 1 decoder layer)",
+        "model_time": how,
+        "cpu_baseline": {"value": value, "unit": "weights/s", "cores": ref.cores, "kind": "port",
+                         "sample": "%d timed steps of one linear layer each (CPU oracle, %d threads)" % (
+                             args.steps, ref.cores)},
         "e2e": {"value": value, "unit": "weights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is a Rust crate and no Rust toolchain exists on this image; the timed CPU path is "
-                "the C++ restatement of it (oracle/), run with all host threads",
+                "the C++ restatement of it (oracle/), run with all host threads (sched_getaffinity), like the "
+                "reference's rayon pool",
     }
     print(json.dumps(line), flush=True)
 
@@ -816,7 +906,8 @@ def main():
             "peaks_file": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")},
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_sample(layers[:7], inputs[:4], H[:4], W[:7], cfg)
+            line["cpu_baseline"], ref_results = cpu_baseline_sample(layers[:7], inputs[:4], H[:4], W[:7], cfg)
+            line["parity"] = parity_report(ref_results, batch, layers)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -49,13 +49,30 @@ def assign_factorisations(ns, world, power=3):
     return owner
 
 
-def exchange_factors(factors, owner):
+def exchange_factors(factors, owner, stream_handle=None):
     """Broadcast every factor from its owner rank, inputs in index order (every rank takes the same collective
-    steps in the same order).  `factors` are tensors on the process group's device."""
+    steps in the same order).  `factors` are tensors on the process group's device.
+
+    The collectives are ordered after torch's current stream.  When the factors were written on another stream
+    (`stream_handle`, the library's stream: 0 = the legacy default stream), the current stream first waits for
+    that stream, and afterwards that stream waits for the broadcasts, so the library reads every factor only
+    once it has landed."""
+    import torch
     import torch.distributed as dist
 
+    cur = torch.cuda.current_stream() if stream_handle is not None else None
+    other = None
+    if cur is not None and stream_handle != cur.cuda_stream:
+        other = torch.cuda.ExternalStream(stream_handle) if stream_handle else torch.cuda.default_stream()
+        ev = torch.cuda.Event()
+        ev.record(other)
+        cur.wait_event(ev)
     for i, u in enumerate(factors):
         dist.broadcast(u, src=owner[i])
+    if other is not None:
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        other.wait_event(ev)
 
 
 class ModelBatch:
@@ -193,7 +210,7 @@ class ModelBatch:
                                                     ctypes.cast(self._lwhich, ctypes.c_void_p), len(self.lmine),
                                                     ctypes.byref(c), ctypes.cast(self._lu_out, ctypes.c_void_p), dev,
                                                     ctypes.c_void_p(stream_handle)))
-            exchange_factors(self.lu, self.lowner)
+            exchange_factors(self.lu, self.lowner, stream_handle)
             check(lib().cdclq_quantize_batch(self.ins, len(self.ins), self.lys, len(self.lys), ctypes.byref(c), dev,
                                              ctypes.c_void_p(stream_handle)))
             return
@@ -203,6 +220,6 @@ class ModelBatch:
             return
         check(lib().cdclq_prepare_factors(self.ins, len(self.ins), self.which, len(self.mine), ctypes.byref(c),
                                           self.u_out, dev, ctypes.c_void_p(stream_handle)))
-        exchange_factors(self.u, self.owner)
+        exchange_factors(self.u, self.owner, stream_handle)
         check(lib().cdclq_quantize_batch_prepared(self.ins, len(self.ins), self.u_in, self.lys, len(self.lys),
                                                   ctypes.byref(c), dev, ctypes.c_void_p(stream_handle)))

@@ -393,6 +393,32 @@ static int factor_finish(FactorGroup& g) {
     return 0;
 }
 
+// Test and tuning overrides, read at every call from the environment (unset = the automatic choice):
+//   CDCLQ_FACTOR_BUDGET_BYTES  caps the device memory the factorisations may use at once, so a batch of
+//                              inputs is factorised in memory-bounded sub-batches as on a full device;
+//   CDCLQ_REPAIR_LAYOUT        the repair launch layout: "passes" (one launch per pass over 64-row slices),
+//                              "single" (persistent, one CTA per chunk), "pairs" (persistent, each chunk over a
+//                              2-CTA cluster of 64-row tiles), "split" (the widest layers' chunks as SM-owning
+//                              clusters beside a persistent launch of the others).
+// Every layout gives the same codes, scales, zero points and pass counts.
+static size_t env_size(const char* name) {
+    const char* s = getenv(name);
+    if (!s || !*s) return 0;
+    return (size_t)strtoull(s, nullptr, 10);
+}
+
+enum RepairLayout { LAYOUT_AUTO = -1, LAYOUT_PASSES = 0, LAYOUT_SINGLE = 1, LAYOUT_PAIRS = 2, LAYOUT_SPLIT = 3 };
+
+static int repair_layout_override() {
+    const char* s = getenv("CDCLQ_REPAIR_LAYOUT");
+    if (!s || !*s) return LAYOUT_AUTO;
+    if (!strcmp(s, "passes")) return LAYOUT_PASSES;
+    if (!strcmp(s, "single")) return LAYOUT_SINGLE;
+    if (!strcmp(s, "pairs")) return LAYOUT_PAIRS;
+    if (!strcmp(s, "split")) return LAYOUT_SPLIT;
+    return LAYOUT_AUTO;
+}
+
 // Factorise every group.  Groups of different widths are independent: when their work matrices fit in
 // free memory together they run concurrently on separate streams (the latency-bound panel steps of one
 // width overlap the other's); otherwise each group runs alone in memory-bounded sub-batches.
@@ -414,6 +440,7 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
         }
     }
     size_t budget = freeb > ((size_t)4 << 30) ? freeb - ((size_t)4 << 30) : freeb / 2;
+    if (size_t cap = env_size("CDCLQ_FACTOR_BUDGET_BYTES")) budget = std::min(budget, cap);
     size_t need = 0;
     for (auto& g : groups) need += factor_item_bytes(g.n, g.h32_only) * g.hs.size();
     cudaEvent_t ready = nullptr;
@@ -904,7 +931,8 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     // height.
     size_t max_rows = 0;
     for (auto& P : plans) max_rows = std::max(max_rows, std::min(P.rc, P.d_out));
-    const bool persistent = total_chunks >= (size_t)sms;
+    const int layout = repair_layout_override();
+    const bool persistent = layout == LAYOUT_AUTO ? total_chunks >= (size_t)sms : layout != LAYOUT_PASSES;
     if (cdcl && (rp.do_cd || rp.do_refit) && persistent) {
         int* counter = nullptr;
         if ((rc = ar.alloc(&counter, 1))) return rc;
@@ -954,6 +982,17 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
                         split = (int)nh;
                         split_sms = s_h;
                     }
+                }
+            }
+            if (layout == LAYOUT_SINGLE) mode = 0;
+            if (layout == LAYOUT_PAIRS) mode = 1;
+            if (layout == LAYOUT_SPLIT) {
+                if (nh < total_chunks) {  // the widest layers' chunks apart, each cluster CTA on its own SM
+                    mode = 2;
+                    split = (int)nh;
+                    split_sms = (int)std::max<size_t>(2, std::min<size_t>(2 * nh, (size_t)sms / 2)) & ~1;
+                } else {
+                    mode = 0;  // one width only: nothing to split off
                 }
             }
             if (mode == 1) {

@@ -6,8 +6,15 @@
 // running inside a framework whose allocator already owns the device memory (an extra cudaMalloc there can
 // fail or fragment the framework's pool), or a runtime that reserves all of its memory at start-up and
 // forbids allocation afterwards.  This file gives them a variant whose scratch is a file-scope
-// `__device__` array of fixed size, set aside when the library is loaded and kept by every GPU that loads
-// it until the process exits.
+// `__device__` array of fixed size, kept by every GPU that uses it until the process exits.
+//
+// When the array's device memory is reserved: with CUDA's lazy module loading (the default since CUDA 12.2,
+// CUDA_MODULE_LOADING=LAZY) this file's module is loaded into a device's context - and the 4 MiB array
+// reserved there - only when something of the module is first needed on that device, here the
+// cudaGetSymbolAddress of the first call.  That first call per device can therefore itself take device
+// memory (the module and the array); a caller that forbids allocation after start-up makes that first call at
+// start-up (a call with t = 0 resolves the scratch and launches nothing), before any stream capture.  With
+// CUDA_MODULE_LOADING=EAGER the module, array included, is loaded with the context.
 //
 // The caller still owns and passes the inputs (x, y) and the output (h); only the scratch is internal.
 #include <mutex>
@@ -57,8 +64,9 @@ extern "C" int cdclq_gram_accumulate_device_noalloc(const float* x, const float*
                                             "(at most " + std::to_string(kNoAllocGramMaxN) + " columns); use "
                                             "cdclq_gram_accumulate_device");
     float* tmp = nullptr;
-    int rc = noalloc_scratch(&tmp);
+    int rc = noalloc_scratch(&tmp);  // first call on a device: loads the module, reserves the array
     if (rc) return rc;
+    if (t == 0) return 0;  // nothing to add: a start-up call that only resolves the scratch
     // Every element of the scratch that a chunk reads is written by the same chunk's GEMM first (beta = 0;
     // for x == y the widening reads only the lower triangle, which the GEMM always writes), so the previous
     // call's contents never leak into a result and nothing needs clearing.

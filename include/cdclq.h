@@ -5,8 +5,8 @@
  *     engine::quantize_layer(w, d_out, d_in, h, m, hkey, cfg, cache) -> Result<(QLayer, LayerStats)>
  * (src/engine.rs:690-699), built on linalg.rs (Cholesky, triangular inverse, U factor, Gram accumulation)
  * and quant.rs (grid, code).  Every entry point below replaces one of those functions; the comment on each
- * cites the reference function it stands in for.  A Rust caller binds them with `extern "C"` (see
- * INTEGRATION.md); Python binds them with ctypes (cdcl-gptq_b200/cdclq/_lib.py).
+ * cites the reference function it stands in for.  A Rust caller binds them with an `extern "C"` block;
+ * Python binds them with ctypes (cdcl-gptq_b200/cdclq/_lib.py).
  *
  * Conventions shared by all entry points
  *  - Plain pointers and sizes only.  Matrices are row-major.  Functions without a `_device` suffix take HOST
@@ -243,9 +243,12 @@ int cdclq_gram_accumulate_device(const float* x, const float* y, size_t t, size_
  * exits).  For callers that cannot call cudaMalloc where they accumulate a Hessian - a hook inside a
  * framework whose allocator owns the device memory, or a runtime that forbids allocation after start-up.
  * The caller passes device pointers for x, y and h.  n above CDCLQ_NOALLOC_GRAM_MAX_N returns CDCLQ_ERR_ARG.
- * The first call on each device looks up the scratch's device address (cudaGetSymbolAddress); make that
- * first call before any stream capture.  All calls share the one scratch: calls that overlap on the GPU
- * (other streams, other host threads) race and must be serialised by the caller. */
+ * The first call on each device looks up the scratch's device address (cudaGetSymbolAddress); under CUDA's
+ * default lazy module loading that first call is also when the library's module and the 4 MiB array are
+ * loaded into the device's memory, so it can itself take device memory: make it at start-up (t = 0 only
+ * resolves the scratch and computes nothing) and before any stream capture.  All calls share the one
+ * scratch: calls that overlap on the GPU (other streams, other host threads) race and must be serialised
+ * by the caller. */
 #define CDCLQ_NOALLOC_GRAM_MAX_N 1024
 int cdclq_gram_accumulate_device_noalloc(const float* x, const float* y, size_t t, size_t n, double* h,
                                          void* stream);

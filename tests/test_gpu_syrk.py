@@ -139,3 +139,38 @@ def test_f16_gram_matches_exact_within_f32_chunk_error(gpu):
     bound = ((t + 2047) // 2048) * 2048 * 2.0 ** -24 * ab + 1e-12
     assert np.all(np.abs(got - ex) <= bound)
     assert np.array_equal(got, got.T)
+
+
+# the widths of configs[3]'s inputs (4096: q/k/v/o and gate/up; 11008: down_proj), whose SYRK outputs feed the
+# quantizer inside the north-star run: a wave or more of output tiles, ragged tiles at 11008 = 43 * 256, a partial
+# last token chunk at t = 5100
+@pytest.mark.parametrize("t,n", [(5100, 4096), (4096, 11008)])
+def test_bf16_gram_wide_matches_exact_within_f32_chunk_error(gpu, t, n):
+    import torch
+
+    from cdclq import linalg
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(31 + n)
+    scale = torch.exp(torch.randn(n, generator=g, device="cuda"))
+    x = (torch.randn(t, n, generator=g, device="cuda") * scale).to(torch.bfloat16)
+    xd = x.double()
+    ex = xd.T @ xd  # bf16 x bf16 products are exact in f64; f64 sums err by ~t * 2^-53, far inside the bound
+    ab = xd.abs().T @ xd.abs()
+    del xd
+    h = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_bf16_device(x, h)
+    torch.cuda.synchronize()
+    chunks = (t + 2047) // 2048
+    bound = ab.mul_(chunks * 2048 * 2.0 ** -24).add_(1e-12)
+    err = (h - ex).abs_()
+    ratio = float((err / bound).max())
+    assert ratio <= 1.0, ratio
+    del err, bound
+    h32 = torch.zeros(n, n, dtype=torch.float64, device="cuda")
+    linalg.gram_accumulate_device(x.float().contiguous(), h32)  # the reference's arithmetic (bit-exact f32 path)
+    torch.cuda.synchronize()
+    e_tc = float(torch.linalg.norm(h - ex))
+    e_f32 = float(torch.linalg.norm(h32 - ex))
+    assert e_tc <= 3.0 * e_f32 + 1e-9 * float(torch.linalg.norm(ex)), (e_tc, e_f32)
+    assert torch.equal(h, h.T)  # the upper triangle mirrors the lower one exactly

@@ -54,3 +54,15 @@ def test_noalloc_gram_rejects_width_above_capacity(gpu):
                                                           ctypes.c_void_p(h.data_ptr()), None)
     assert rc == -3
     assert "exceeds the allocation-free scratch" in cdclq.lib().cdclq_last_error().decode()
+
+
+def test_noalloc_gram_startup_call_with_no_tokens(gpu):
+    """A start-up call with t = 0 (what a runtime that forbids later allocation makes once per device, so that the
+    module and its scratch are loaded then) succeeds and leaves H untouched."""
+    import torch
+
+    n = 64
+    x = torch.zeros(1, n, device="cuda")
+    h = torch.full((n, n), 3.0, dtype=torch.float64, device="cuda")
+    _call("cdclq_gram_accumulate_device_noalloc", x, x, 0, n, h, torch)
+    assert bool((h == 3.0).all())
