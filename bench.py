@@ -210,6 +210,58 @@ def load_peaks():
 
 
 # ------------------------------------------------------------------------------------------------------------
+class RuntimeBatch:
+    """Descriptor tables of the model for cdclq_runtime_quantize_batch: FULL layers on every rank (each rank
+    quantizes its rows), inputs and outputs on the device (on_device=True) or in pinned host memory.
+
+    h2d_bytes / d2h_bytes count what this rank copies per step in the host mode: the Hessians it owns (the
+    runtime uploads each Hessian once, on its owner, and broadcasts it), its rows of every W, and its rows of
+    codes, scales and zero points back (rank 0: every row, gathered over NVLink)."""
+
+    def __init__(self, torch, rt, layers, inputs, H, W, cfg, on_device):
+        from cdclq.abi import CBatchInput, CBatchLayer, CLayerStats, num_groups
+        from cdclq.runtime import assign_owners, shard_rows
+
+        self.rt, self.cfg, self.on_device = rt, cfg, on_device
+        self.keep = list(H) + list(W)
+        self.ins = (CBatchInput * len(inputs))()
+        for i, (_, n) in enumerate(inputs):
+            self.ins[i].h = H[i].data_ptr()
+            self.ins[i].n = n
+        self.lys = (CBatchLayer * len(layers))()
+        self.stats = [CLayerStats() for _ in layers]
+        self.outs = []
+        self.layer_index = list(range(len(layers)))
+        dev = "cuda" if on_device else "cpu"
+        owner = assign_owners([n for (_, n) in inputs], rt.nranks, 3)
+        self.h2d_bytes = sum(n * n * 4 for i, (_, n) in enumerate(inputs) if owner[i] == rt.rank)
+        self.d2h_bytes = 0
+        for li, (name, d_out, d_in, inp) in enumerate(layers):
+            ng = num_groups(cfg, d_in)
+            o = dict(perm=np.zeros(d_in, np.uint32), gbits=np.zeros(ng, np.uint8),
+                     codes=torch.empty(d_out, d_in, dtype=torch.uint8, device=dev, pin_memory=not on_device),
+                     scales=torch.empty(d_out, ng, dtype=torch.float32, device=dev, pin_memory=not on_device),
+                     zeros=torch.empty(d_out, ng, dtype=torch.float32, device=dev, pin_memory=not on_device))
+            self.outs.append(o)
+            L = self.lys[li]
+            L.w = W[li].data_ptr()
+            L.d_out = d_out
+            L.input = inp
+            L.perm = o["perm"].ctypes.data
+            L.gbits = o["gbits"].ctypes.data
+            L.codes = o["codes"].data_ptr()
+            L.scales = o["scales"].data_ptr()
+            L.zeros = o["zeros"].data_ptr()
+            L.stats = ctypes.pointer(self.stats[li])
+            r0, r1 = shard_rows(d_out, cfg.row_chunk, rt.rank, rt.nranks, li)
+            self.h2d_bytes += (r1 - r0) * d_in * 4
+            rows = d_out if rt.rank == 0 else r1 - r0
+            self.d2h_bytes += rows * d_in + 2 * rows * ng * 4
+
+    def run(self, gather):
+        self.rt.quantize_batch(self.ins, self.lys, self.cfg, self.on_device, gather)
+
+
 def host_cores():
     """Host CPU threads this process may run on (the affinity mask, not OMP_NUM_THREADS: torchrun sets that
     to 1 for every rank)."""
@@ -803,22 +855,24 @@ def main():
         return
 
     import cdclq
-    from cdclq.pipeline import ModelBatch
+    from cdclq.runtime import Runtime
 
     cdclq.lib()
     cfg = bench_config()
     device = "cuda"
     layers, inputs, H, W = generate(torch, device, args.layers)
     total_weights = sum(l[1] * l[2] for l in layers)
-    batch = ModelBatch(torch, layers, inputs, H, W, cfg, rank, world, on_device=True)
-    stream = torch.cuda.current_stream()
+    # the library's runtime on every N: one rank per GPU, its own NCCL communicator (factor broadcasts grouped)
+    rt = Runtime.from_process_group(device=local) if world > 1 else Runtime(device=0)
+    batch = RuntimeBatch(torch, rt, layers, inputs, H, W, cfg, on_device=True)
+    stream = torch.cuda.ExternalStream(rt.stream_handle)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
     for _ in range(args.warmup):
-        batch.run(stream.cuda_stream)
+        batch.run(gather=False)
     torch.cuda.synchronize()
     barrier()
     launches0 = cdclq.lib().cdclq_launch_count()
@@ -830,7 +884,7 @@ def main():
     e0.record(stream)
     profiles = []
     for _ in range(args.steps):
-        batch.run(stream.cuda_stream)
+        batch.run(gather=False)
         profiles.append(cdclq._lib.last_run_profile())
     e1.record(stream)
     torch.cuda.synchronize()
@@ -842,25 +896,21 @@ def main():
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-        # per-layer losses of the row shards are additive: all-reduce the model totals
-        lt = torch.tensor([sum(s.loss_gptq for s in batch.stats), sum(s.loss_final for s in batch.stats)],
-                          dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(lt)
-        loss_gptq, loss_final = float(lt[0]), float(lt[1])
-    else:
-        loss_gptq = sum(s.loss_gptq for s in batch.stats)
-        loss_final = sum(s.loss_final for s in batch.stats)
+    # the runtime all-reduces every layer's statistics: every rank holds the model totals
+    loss_gptq = sum(s.loss_gptq for s in batch.stats)
+    loss_final = sum(s.loss_final for s in batch.stats)
 
-    # ---- e2e through the public C ABI with pinned host buffers
+    # ---- e2e through the public C ABI with pinned host buffers: each Hessian uploaded by its owner rank and
+    # broadcast over NVLink, each rank uploading its rows of W, outputs gathered on rank 0 and copied to the host
     Hh = [h.cpu().pin_memory() for h in H]
     Wh = [w.cpu().pin_memory() for w in W]
-    hb = ModelBatch(torch, layers, inputs, Hh, Wh, cfg, rank, world, on_device=False)
-    hb.run(0)  # warm the host path once
+    hb = RuntimeBatch(torch, rt, layers, inputs, Hh, Wh, cfg, on_device=False)
+    hb.run(gather=True)  # warm the host path once
     torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        hb.run(0)
+        hb.run(gather=True)
     torch.cuda.synchronize()
     e2e_s = (time.perf_counter() - t0) / args.e2e_steps
     e2e_prof = cdclq._lib.last_run_profile()
@@ -885,6 +935,8 @@ def main():
             "config": workload_config(cfg),
             "e2e": {"value": total_weights / e2e_s, "unit": "weights/s", "seconds_per_model": e2e_s,
                     "h2d_bytes_per_step": hb.h2d_bytes, "d2h_bytes_per_step": hb.d2h_bytes,
+                    "bytes_scope": "rank 0: the Hessians it owns (each uploaded once, then broadcast over NVLink) and "
+                                   "its rows of W in; every row's codes, scales and zero points out (gathered)",
                     "phases_ms": {k: e2e_prof[k] for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair",
                                                            "ms_final")}},
             "gpu_launches": int(launches),
@@ -909,6 +961,7 @@ def main():
             line["cpu_baseline"], ref_results = cpu_baseline_sample(layers[:7], inputs[:4], H[:4], W[:7], cfg)
             line["parity"] = parity_report(ref_results, batch, layers)
         print(json.dumps(line), flush=True)
+    rt.close()  # every rank: the library's communicator is released before the process group
     if world > 1:
         torch.distributed.destroy_process_group()
 

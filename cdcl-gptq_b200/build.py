@@ -20,8 +20,8 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "cdclq", "libcdclq_cuda.so")
 SOURCES = ["engine.cu", "prep.cu", "gptq.cu", "repair.cu", "repair_bm64.cu", "repair_bm128.cu", "gemm.cu", "pack.cu",
-           "syrk.cu", "noalloc.cu", "io.cu"]
-HEADERS = ["common.cuh", "gemm_core.cuh", "kernels.h", "repair_core.cuh"]
+           "syrk.cu", "noalloc.cu", "io.cu", "model_io.cu", "runtime.cu", "model.cu"]
+HEADERS = ["common.cuh", "gemm_core.cuh", "kernels.h", "repair_core.cuh", "model_io.h", "runtime.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC"]
 
@@ -105,7 +105,7 @@ def build(verbose=False, force=False):
                 failed.append(src)
     if failed:
         raise RuntimeError("nvcc failed on %s" % ", ".join(failed))
-    cmd = [nvcc_path()] + ARCH + ["-shared", "-o", OUT] + [_obj(s) for s in SOURCES]
+    cmd = [nvcc_path()] + ARCH + ["-shared", "-o", OUT] + [_obj(s) for s in SOURCES] + ["-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stdout.write(r.stdout)

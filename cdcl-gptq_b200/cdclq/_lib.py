@@ -6,7 +6,7 @@ raises.  Loading the library does not need a GPU; computing does (the C ABI retu
 import ctypes
 import os
 
-from .abi import CBatchInput, CBatchLayer, CConfig, CLayerStats, CRunProfile
+from .abi import CBatchInput, CBatchLayer, CConfig, CLayerStats, CModelOpts, CModelReport, CRunProfile
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcdclq_cuda.so")
@@ -58,6 +58,17 @@ SIGNATURES = {
     "cdclq_row_bytes": (SZ, [SZ, SZ, P]),
     "cdclq_pack": (I32, [P, SZ, SZ, SZ, P, P]),
     "cdclq_unpack_dequant": (I32, [P, SZ, SZ, SZ, P, P, P, P, P]),
+    "cdclq_runtime_unique_id": (I32, [P]),
+    "cdclq_runtime_create": (I32, [I32, I32, I32, P, ctypes.c_double, ctypes.POINTER(P)]),
+    "cdclq_runtime_destroy": (None, [P]),
+    "cdclq_runtime_stream": (P, [P]),
+    "cdclq_runtime_quantize_batch": (I32, [P, ctypes.POINTER(CBatchInput), SZ, ctypes.POINTER(CBatchLayer), SZ, CFG, I32,
+                                           I32]),
+    "cdclq_shard_rows": (None, [SZ, SZ, I32, I32, SZ, ctypes.POINTER(SZ), ctypes.POINTER(SZ)]),
+    "cdclq_assign_owners": (None, [P, SZ, I32, I32, P]),
+    "cdclq_quantize_model": (I32, [P, ctypes.POINTER(CModelOpts), ctypes.POINTER(CModelReport)]),
+    "cdclq_dequantize_packed": (I32, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                      ctypes.POINTER(ctypes.c_uint64)]),
     "cdclq_launch_count": (ctypes.c_uint64, []),
     "cdclq_last_run_profile": (I32, [ctypes.POINTER(CRunProfile)]),
     "cdclq_version": (ctypes.c_char_p, []),

@@ -79,6 +79,39 @@ class CBatchLayer(ctypes.Structure):
     ]
 
 
+class CModelOpts(ctypes.Structure):
+    """`cdclq_model_opts` (include/cdclq.h)."""
+
+    _fields_ = [
+        ("weights", ctypes.POINTER(ctypes.c_char_p)),
+        ("n_weights", ctypes.c_size_t),
+        ("hessians", ctypes.POINTER(ctypes.c_char_p)),
+        ("n_hessians", ctypes.c_size_t),
+        ("out_dir", ctypes.c_char_p),
+        ("only", ctypes.POINTER(ctypes.c_char_p)),
+        ("n_only", ctypes.c_size_t),
+        ("skip", ctypes.POINTER(ctypes.c_char_p)),
+        ("n_skip", ctypes.c_size_t),
+        ("emit_packed", ctypes.c_int32),
+        ("emit_dequant", ctypes.c_int32),
+        ("verbose", ctypes.c_int32),
+        ("pad", ctypes.c_int32),
+        ("cfg", CConfig),
+    ]
+
+
+class CModelReport(ctypes.Structure):
+    """`cdclq_model_report` (include/cdclq.h)."""
+
+    _fields_ = [
+        ("layers", ctypes.c_uint64),
+        ("total_loss_gptq", ctypes.c_double),
+        ("total_loss_final", ctypes.c_double),
+        ("total_gain_pct", ctypes.c_double),
+        ("total_secs", ctypes.c_double),
+    ]
+
+
 class CRunProfile(ctypes.Structure):
     """`cdclq_run_profile` (include/cdclq.h)."""
 

@@ -1147,7 +1147,34 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     return CDCLQ_OK;
 }
 
-static int ensure_device() {
+// Permutation, group widths and skeleton group count of a layer (src/engine.rs:271-304, 761-763) from its
+// Hessian on the device and, with a skeleton, the column scores of its full weight matrix (host, n f64, original
+// order; null without a skeleton).  What cdclq_quantize_batch computes for the layer; the multi-GPU runtime
+// uses it on every rank, rows or not, so that each rank reports every layer's permutation.
+int layer_perm(const float* h_dev, size_t n, const double* colsq, const cdclq_config& cfg, std::vector<uint32_t>& perm,
+               std::vector<uint8_t>& gbits, size_t& nskel, cudaStream_t st) {
+    double* hd = nullptr;
+    CDCLQ_CUDA_TRY(cudaMallocAsync(&hd, n * sizeof(double), st));
+    int rc = launch_hdiag(h_dev, (int)n, hd, st);
+    std::vector<double> hdiag(n);
+    if (!rc) {
+        cudaError_t e = cudaMemcpyAsync(hdiag.data(), hd, n * sizeof(double), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = cuda_error(e, "hdiag read-back");
+    }
+    cudaFreeAsync(hd, st);
+    if (rc) return rc;
+    const size_t g = effective_group(cfg, n);
+    std::vector<double> cs;
+    if (colsq) cs.assign(colsq, colsq + n);
+    compute_perm(hdiag, colsq ? &cs : nullptr, n, g, cfg, perm, nskel);
+    const size_t ng = (n + g - 1) / g;
+    gbits.resize(ng);
+    for (size_t gi = 0; gi < ng; gi++) gbits[gi] = (uint8_t)(gi < nskel ? cfg.skeleton_bits : cfg.bits);
+    return 0;
+}
+
+int ensure_device() {
     int count = 0;
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count == 0)

@@ -6,7 +6,10 @@
 //   2. columns are processed in order.  Four threads share a row: they compute the group grid together at a
 //      group start (min/max split four ways, the 24 MSE clip candidates split four ways), quantize the
 //      column redundantly, and split the rank-1 in-block compensation w1[:, j+1:i2] -= eps * U[j, j+1:i2]
-//      four ways.  The four lanes sit in one warp, so a __syncwarp orders consecutive columns;
+//      four ways.  The four lanes sit in one warp, so a __syncwarp orders consecutive columns.  The rows of U
+//      the compensation reads come from a shared-memory window of P1_UWIN rows, double-buffered with cp.async
+//      (the next window is in flight while the current one is used), so no global load sits inside the
+//      column-to-column dependency chain;
 //   3. the deferred compensation w[:, i2:] -= err1 * U[i1:i2, i2:] runs on the FP32 GEMM core
 //      (A = err1 from shared memory, B = U tiles), one subtraction per element per block as in the reference.
 // Outputs per element: code, dequantized value, and eps^2 (consumed by the per-chunk conflict statistics).
@@ -25,6 +28,41 @@ constexpr int P1_W1LD = 72;
 constexpr int P1_ELD = P1Tile::ALD;  // err1 stride (16-byte aligned k-major A operand)
 
 static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// U window: up to P1_UWIN rows of U[j, i1:i1+B] per buffer, two buffers in the lazy GEMM's B staging area
+// (unused during the column loop): 2 * 16 * 128 floats = the Tile's B_STAGE_FLOATS; wider blocks get fewer rows.
+constexpr int P1_UWIN = 16;
+static_assert(2 * P1_UWIN * 128 <= P1Tile::B_STAGE_FLOATS, "the U window must fit the staging buffer");
+__host__ __device__ inline int p1_uwin(int B) {
+    int w = (P1Tile::B_STAGE_FLOATS / 2) / B;
+    return w < 1 ? 1 : (w > P1_UWIN ? P1_UWIN : w);
+}
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Rows j0 .. j0+rows-1 of U, columns i1 .. i1+cnt-1, into win[(j - j0) * B + k].  16-byte copies when every row
+// segment is 16-byte aligned (n and i1 multiples of 4; the block width B is), plain loads otherwise.
+__device__ __forceinline__ void load_u_window(float* win, const float* U, int n, int i1, int j0, int rows, int cnt,
+                                              int B, bool vec, int tid) {
+    if (vec) {
+        const int q = (cnt + 3) >> 2;  // 16-byte segments per row (cnt % 4 == 0 here)
+        for (int idx = tid; idx < rows * q; idx += GEMM_THREADS) {
+            const int rr = idx / q, c4 = (idx - rr * q) << 2;
+            cp_async16(win + rr * B + c4, U + (int64_t)(j0 + rr) * n + i1 + c4);
+        }
+        cp_async_commit();
+    } else {
+        for (int idx = tid; idx < rows * cnt; idx += GEMM_THREADS) {
+            const int rr = idx / cnt, k = idx - rr * cnt;
+            win[rr * B + k] = __ldg(U + (int64_t)(j0 + rr) * n + i1 + k);
+        }
+    }
+}
 
 size_t phase1_smem_bytes(int block) {
     size_t b = (size_t)block;
@@ -58,10 +96,22 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
         }
         for (int idx = tid; idx < P1_ELD * cnt; idx += blockDim.x) err1[idx] = 0.0f;
         for (int k = tid; k < cnt; k += blockDim.x) invd[k] = __fdiv_rn(1.0f, __ldg(U + (int64_t)(i1 + k) * n + i1 + k));
-        __syncthreads();
+        const bool uvec = (n % 4 == 0) && (i1 % 4 == 0) && (cnt % 4 == 0);
+        const int uw = p1_uwin(B);
+        load_u_window(stage, U, n, i1, i1, min(uw, cnt), cnt, B, uvec, tid);
 
         for (int i = 0; i < cnt; i++) {
             const int j = i1 + i;
+            if (i % uw == 0) {
+                // window i / uw has landed; every warp is done with the previous one, whose buffer now receives
+                // the next window
+                if (uvec) cp_async_wait_all();
+                __syncthreads();
+                const int nw = i + uw;
+                if (nw < cnt)
+                    load_u_window(stage + ((nw / uw) & 1) * uw * B, U, n, i1, i1 + nw, min(uw, cnt - nw), cnt, B, uvec,
+                                  tid);
+            }
             if (j % g == 0) {
                 // ---- group grid from the weights current at its first column (src/engine.rs:410-423)
                 const int gi = j / g, gend = min(j + g, n);
@@ -149,10 +199,10 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
                 cbuf[i * P1_ROWS + r] = c;
                 w1[i * P1_W1LD + r] = dq;  // column i is final: keep its dequantized value
             }
-            const float* urow = U + (int64_t)j * n + i1;
+            const float* urow = stage + ((i / uw) & 1) * uw * B + (i % uw) * B;  // U[j, i1:i2]
             for (int k = i + 1 + sub; k < cnt; k += 4) {
                 float* x = &w1[k * P1_W1LD + r];
-                *x = __fsub_rn(*x, __fmul_rn(e, __ldg(urow + k)));
+                *x = __fsub_rn(*x, __fmul_rn(e, urow[k]));
             }
             __syncwarp();
         }

@@ -40,6 +40,9 @@ int device_tri_inverse(const double* l, double* y, double* tbuf, int n, cudaStre
 // Weight-side preparation (prep.cu)
 // colsq[j] = sum_r w[r][j]^2 in f64, rows in order, dead columns read as 0 (src/engine.rs:279-285)
 int launch_colsq(const float* w, const double* hdiag, int d_out, int n, double* colsq, cudaStream_t st);
+// the same sums continued from init[j] (in place when init == colsq): a row shard after the rows before it
+int launch_colsq_from(const float* w, const double* hdiag, int d_out, int n, const double* init, double* colsq,
+                      cudaStream_t st);
 // wt[r][j] = dead(perm[j]) ? 0 : w[r][perm[j]]  (src/engine.rs:708-731)
 int launch_permute_w(const float* w, const double* hdiag, const uint32_t* perm, int d_out, int n, float* wt,
                      cudaStream_t st);

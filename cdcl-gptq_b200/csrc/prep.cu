@@ -687,12 +687,13 @@ int launch_hdiag(const float* h, int n, double* hdiag, cudaStream_t st) {
     return e == cudaSuccess ? 0 : cuda_error(e, "hdiag_kernel launch");
 }
 
-// src/engine.rs:279-285 over the dead-zeroed weights: rows summed in order, (w as f64) * (w as f64)
-__global__ void colsq_kernel(const float* w, const double* hdiag, int d_out, int n, double* colsq) {
+// src/engine.rs:279-285 over the dead-zeroed weights: rows summed in order, (w as f64) * (w as f64), starting
+// from init[j] (the running sums of the rows before these, held by another rank) or from 0 when init is null
+__global__ void colsq_kernel(const float* w, const double* hdiag, int d_out, int n, const double* init, double* colsq) {
     int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= n) return;
     bool dead = hdiag[j] == 0.0;
-    double s = 0.0;
+    double s = init ? init[j] : 0.0;
     for (int r = 0; r < d_out; r++) {
         double v = dead ? 0.0 : (double)w[(int64_t)r * n + j];
         s = __dadd_rn(s, __dmul_rn(v, v));
@@ -701,7 +702,12 @@ __global__ void colsq_kernel(const float* w, const double* hdiag, int d_out, int
 }
 
 int launch_colsq(const float* w, const double* hdiag, int d_out, int n, double* colsq, cudaStream_t st) {
-    CDCLQ_LAUNCH(colsq_kernel, (n + 255) / 256, 256, 0, st, w, hdiag, d_out, n, colsq);
+    return launch_colsq_from(w, hdiag, d_out, n, nullptr, colsq, st);
+}
+
+int launch_colsq_from(const float* w, const double* hdiag, int d_out, int n, const double* init, double* colsq,
+                      cudaStream_t st) {
+    CDCLQ_LAUNCH(colsq_kernel, (n + 255) / 256, 256, 0, st, w, hdiag, d_out, n, init, colsq);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "colsq_kernel launch");
 }

@@ -216,6 +216,87 @@ int cdclq_quantize_batch_prepared(const cdclq_batch_input* inputs, size_t n_inpu
                                   const cdclq_batch_layer* layers, size_t n_layers, const cdclq_config* cfg,
                                   int on_device, void* stream);
 
+/* ---- runtime: one process per GPU, the NCCL communicator owned by the library ---------------------------
+ * The reference runs on one host (pipeline::quantize_model over the rayon pool, src/pipeline.rs:79-227,
+ * src/main.rs:199-203).  A runtime is one rank of a multi-GPU job: its device, its stream and, with more than one
+ * rank, its NCCL communicator (NCCL is loaded at run time; a process that already loaded it shares that copy).
+ * Every wait - the communicator's creation included - is bounded by timeout_s; after a timeout or an NCCL
+ * failure the communicator is aborted and later calls on the runtime fail.  Calls are collective: every rank
+ * makes the same calls in the same order.  Not re-entrant. */
+typedef struct cdclq_runtime cdclq_runtime;
+
+#define CDCLQ_UNIQUE_ID_BYTES 128
+/* ncclGetUniqueId: rank 0 calls it and hands the bytes to every rank over any channel of the caller's. */
+int cdclq_runtime_unique_id(uint8_t* id_out);
+/* One rank: binds `device`, creates its stream and, with nranks > 1, joins the communicator of `unique_id`.
+ * timeout_s <= 0 means 600 s. */
+int cdclq_runtime_create(int device, int nranks, int rank, const uint8_t* unique_id, double timeout_s,
+                         cdclq_runtime** out);
+void cdclq_runtime_destroy(cdclq_runtime* rt);
+/* The runtime's CUDA stream (cudaStream_t as void*): every kernel and collective of its calls runs on it, so a
+ * caller times them with events recorded there. */
+void* cdclq_runtime_stream(const cdclq_runtime* rt);
+
+/* cdclq_quantize_batch over the runtime's ranks, with results identical to one GPU's.  The descriptors describe
+ * FULL layers on every rank (w and the outputs point at row 0; a rank reads and writes only its rows): every
+ * layer's rows are split in whole row chunks (the chunk each layer gets on one GPU), contiguous per rank, the
+ * ranks' ranges rotating from layer to layer; each distinct input is factorised by one owner rank and its U
+ * broadcast (per layer with a skeleton, whose column scores are summed over the ranks' rows in row order);
+ * statistics are all-reduced and perm / gbits / stats are filled on every rank.  on_device = 0: host buffers
+ * (an input's Hessian is only read on its owner rank - see cdclq_assign_owners with power 3 - and broadcast);
+ * 1: device buffers on every rank.  gather != 0: rank 0 also receives every other rank's rows of codes, scales
+ * and zero points.  The descriptors' colsq and u fields are not read. */
+int cdclq_runtime_quantize_batch(cdclq_runtime* rt, const cdclq_batch_input* inputs, size_t n_inputs,
+                                 const cdclq_batch_layer* layers, size_t n_layers, const cdclq_config* cfg,
+                                 int on_device, int gather);
+/* The row range [r0, r1) of `rank` for a layer of d_out rows: whole row chunks, contiguous, the range index
+ * rotated by `rotate` (the layer's index in the batch). */
+void cdclq_shard_rows(size_t d_out, size_t row_chunk, int rank, int nranks, size_t rotate, size_t* r0, size_t* r1);
+/* Owner rank of each of `count` items of size ns[i]: longest processing time on ns[i]^power (3: a factorisation),
+ * largest first, ties by index, to the least-loaded rank (ties to the lowest rank). */
+void cdclq_assign_owners(const size_t* ns, size_t count, int nranks, int power, int* owner_out);
+
+/* ---- model level: safetensors in, packed / dequantized safetensors and report.json out -----------------
+ * pipeline::quantize_model (src/pipeline.rs:79-227).  Per weight shard: every 2-D `<layer>.weight` tensor that
+ * passes the only / skip substring filters and has a Hessian (`<layer>.H`, or an alias of one) is quantized;
+ * all such layers of the shard are quantized as one batch (over the runtime's ranks), then rank 0 writes
+ * <out_dir>/dequant/<shard> (same names, shapes and dtypes, values on the grid) and <out_dir>/packed/<shard>
+ * (six tensors per layer: .qweight .scales .qzeros .perm .gbits .gsize; header quantization=cdclq-v1,
+ * orig_dtype, bits), every other tensor copied byte for byte, and <out_dir>/report.json.  Error messages are the
+ * reference's.  rt = NULL: one GPU (the current device). */
+typedef struct cdclq_model_opts {
+    const char* const* weights; /* safetensors shard paths */
+    size_t n_weights;
+    const char* const* hessians; /* Hessian files (later files override earlier ones) */
+    size_t n_hessians;
+    const char* out_dir;
+    const char* const* only; /* substrings; empty = every layer */
+    size_t n_only;
+    const char* const* skip;
+    size_t n_skip;
+    int32_t emit_packed;
+    int32_t emit_dequant;
+    int32_t verbose; /* per-layer progress lines on stderr, as the reference prints them */
+    int32_t pad;
+    cdclq_config cfg;
+} cdclq_model_opts;
+
+/* The Report's totals (src/pipeline.rs:69-76); the per-layer records are in report.json. */
+typedef struct cdclq_model_report {
+    uint64_t layers;
+    double total_loss_gptq;
+    double total_loss_final;
+    double total_gain_pct;
+    double total_secs;
+} cdclq_model_report;
+
+int cdclq_quantize_model(cdclq_runtime* rt, const cdclq_model_opts* opts, cdclq_model_report* report_out);
+
+/* pipeline::dequantize_packed (src/pipeline.rs:239-275): expands every `<layer>.qweight` of a packed shard into
+ * `<layer>.weight` (dtype: `dtype` if not NULL - F32 / F16 / BF16, HF spellings accepted - else the file's
+ * orig_dtype, else F16), drops the companion tensors, copies everything else.  *layers_out = layers expanded. */
+int cdclq_dequantize_packed(const char* input, const char* output, const char* dtype, uint64_t* layers_out);
+
 /* ---- linear-algebra kernels (linalg.rs) ------------------------------------------------------------ */
 
 /* cholesky_lower (src/linalg.rs:200-276): in place on a host n x n f64 matrix; lower triangle = L. */

@@ -131,6 +131,7 @@ def test_wide_batch_heavy_split(gpu, monkeypatch):
     cfg = wc.config(name)
     _, h_light = orc.problem(1, 256, 600, 501)  # 256 wide: the same effective group (128) as the heavy layer
     w_light = orc.rng_normal(502, 38400 * 256, 0.02).reshape(38400, 256)
+    qb, sb = orc.quantize_layer(w_light, 38400, 256, h_light, None, "light", cfg)
     for layout in ("", "split"):
         monkeypatch.setenv("CDCLQ_REPAIR_LAYOUT", layout)
         outs, stats = _batch([h_heavy, np.ascontiguousarray(h_light)], [(0, w_heavy), (1, w_light)], cfg)
@@ -142,7 +143,6 @@ def test_wide_batch_heavy_split(gpu, monkeypatch):
                "subblocks_total": s.subblocks_total, "skeleton_groups": s.skeleton_groups,
                "passes": want["passes"]}  # per-chunk passes are not reported by the batch call
         compare(name, got, want, layout or "auto")
-        qb, sb = orc.quantize_layer(w_light, 38400, 256, h_light, None, "light", cfg)
         o = outs[1]
         assert np.array_equal(o["codes"], qb.codes) and np.array_equal(o["scales"], qb.scales)
         assert np.array_equal(o["zeros"], qb.zeros) and np.array_equal(o["perm"], qb.perm)
@@ -159,8 +159,8 @@ def test_factorisation_sub_batches(gpu, monkeypatch):
     hs = [np.ascontiguousarray(orc.problem(1, n, 2600, 600 + i)[1]) for i in range(3)]
     ws = [orc.rng_normal(610 + i, 128 * n, 0.02).reshape(128, n) for i in range(3)]
     cfg = wc._cfg(bits=3, group=128, mse_grid=True)
-    item = 8 * n * n * 2 + 4 * n * n * 2  # f64 work matrices + f32 factors per input, roughly
-    monkeypatch.setenv("CDCLQ_FACTOR_BUDGET_BYTES", str(int(1.5 * item)))
+    item = 2 * 8 * n * n + 97 * 8 * n + 256  # one input's f64 work matrices (the engine's per-item estimate)
+    monkeypatch.setenv("CDCLQ_FACTOR_BUDGET_BYTES", str(int(1.5 * item)))  # one input per sub-batch
     outs, stats = _batch(hs, [(i, ws[i]) for i in range(3)], cfg)
     prof = cdclq._lib.last_run_profile()
     assert prof["factor_batches"] >= 3, prof["factor_batches"]
