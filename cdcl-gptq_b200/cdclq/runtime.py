@@ -28,6 +28,28 @@ from .abi import CBatchInput, CBatchLayer, CModelOpts, CModelReport, Config
 UNIQUE_ID_BYTES = 128
 
 
+def _prefer_framework_nccl():
+    """Points the library at the NCCL that torch loads (the pip package nvidia-nccl), unless the caller chose one:
+    the library opens NCCL at its first runtime, and a process that creates a runtime before importing torch would
+    otherwise hold the system's libnccl.so.2 under the soname torch needs for its own, newer copy."""
+    if os.environ.get("CDCLQ_NCCL_LIBRARY"):
+        return
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+        for d in (spec.submodule_search_locations or []) if spec else []:
+            p = os.path.join(d, "lib", "libnccl.so.2")
+            if os.path.exists(p):
+                os.environ["CDCLQ_NCCL_LIBRARY"] = p
+                return
+    except Exception:
+        pass
+
+
+_prefer_framework_nccl()
+
+
 def shard_rows(d_out, row_chunk, rank, nranks, rotate=0):
     """[r0, r1) of `rank`: whole row chunks, contiguous, rotated by `rotate` (cdclq_shard_rows)."""
     r0, r1 = ctypes.c_size_t(0), ctypes.c_size_t(0)

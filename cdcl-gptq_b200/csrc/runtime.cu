@@ -8,8 +8,9 @@
 // distinct inputs' factorisations are spread over the ranks and each factor U is broadcast from its owner over
 // NVLink, and the per-layer statistics are all-reduced.  Results equal a single-GPU run's.
 //
-// NCCL is resolved at run time (dlopen of libnccl.so.2): a process that already loaded NCCL (torch) shares that
-// copy, and the library has no link-time dependency on it.  The communicator is non-blocking, so that every wait
+// NCCL is resolved at run time (dlopen): a process that already loaded NCCL (torch) shares that copy, a process
+// that has not yet loads the copy CDCLQ_NCCL_LIBRARY names (else libnccl.so.2 from the loader's path), and the
+// library has no link-time dependency on it.  The communicator is non-blocking, so that every wait
 // - communicator creation included - is bounded by the runtime's timeout; on a timeout or an NCCL failure the
 // communicator is aborted and every call on the runtime fails from then on.
 #include <dlfcn.h>
@@ -57,7 +58,13 @@ Nccl& nccl() {
     static Nccl api;
     static std::once_flag once;
     std::call_once(once, [] {
-        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        // an NCCL already in the process first (a framework's: a second copy under the same soname would shadow
+        // the one the framework needs), then CDCLQ_NCCL_LIBRARY (a path: the copy the caller's framework will
+        // load), then the loader's search path
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        const char* env = getenv("CDCLQ_NCCL_LIBRARY");
+        if (!h && env && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
         if (!h) {
             api.why = std::string("NCCL not found (libnccl.so.2): ") + dlerror();

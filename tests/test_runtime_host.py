@@ -71,3 +71,19 @@ def test_model_requires_an_output():
         quantize_model(QuantOpts(["m.safetensors"], ["h.safetensors"], "/tmp/none", emit_packed=False,
                                  emit_dequant=False))
     assert str(ei.value) == "nothing to write: both --no-packed and --no-dequant are set"
+
+
+def test_runtime_first_then_torch_shares_one_nccl():
+    """A process that opens the runtime's NCCL before importing torch (a Rust or C caller embedding Python, a
+    worker that builds its runtime first) must still be able to import torch: the library opens the NCCL copy
+    torch will use, not the first libnccl.so.2 on the loader's path."""
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    code = ("import sys; sys.path.insert(0, %r); import cdclq.runtime as r; assert len(r.unique_id()) == 128; "
+            "import torch; print('ok')") % os.path.join(ROOT, "cdcl-gptq_b200")
+    env = {k: v for k, v in os.environ.items() if k != "CDCLQ_NCCL_LIBRARY"}
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-2000:]
