@@ -1068,6 +1068,7 @@ def main():
             "phases_ms": {k: prof[k] for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair", "ms_final")},
             "phase1_tflops": p1_tflops,
             "factorisations": prof["factorisations"], "repair_pass_launches": prof["repair_launches"],
+            "repair_layout": prof["repair_layout"],
             "loss_gptq": loss_gptq, "loss_final": loss_final,
             "clocks": clk,
             "peaks_file": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")},

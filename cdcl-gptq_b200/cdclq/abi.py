@@ -131,6 +131,7 @@ class CRunProfile(ctypes.Structure):
         ("launches", ctypes.c_uint64),
         ("factor_batches", ctypes.c_uint64),
         ("ms_host", ctypes.c_double),
+        ("repair_layout", ctypes.c_uint64),
     ]
 
     def as_dict(self):

@@ -399,7 +399,8 @@ static int factor_finish(FactorGroup& g) {
 //   CDCLQ_REPAIR_LAYOUT        the repair launch layout: "passes" (one launch per pass over 64-row slices),
 //                              "single" (persistent, one CTA per chunk), "pairs" (persistent, each chunk over a
 //                              2-CTA cluster of 64-row tiles), "split" (the widest layers' chunks as SM-owning
-//                              clusters beside a persistent launch of the others).
+//                              clusters beside a persistent launch of the others), "quads" (the same with the
+//                              widest layers' chunks over 4-CTA clusters that also split every GEMM's columns).
 // Every layout gives the same codes, scales, zero points and pass counts.
 static size_t env_size(const char* name) {
     const char* s = getenv(name);
@@ -407,7 +408,9 @@ static size_t env_size(const char* name) {
     return (size_t)strtoull(s, nullptr, 10);
 }
 
-enum RepairLayout { LAYOUT_AUTO = -1, LAYOUT_PASSES = 0, LAYOUT_SINGLE = 1, LAYOUT_PAIRS = 2, LAYOUT_SPLIT = 3 };
+enum RepairLayout {
+    LAYOUT_AUTO = -1, LAYOUT_PASSES = 0, LAYOUT_SINGLE = 1, LAYOUT_PAIRS = 2, LAYOUT_SPLIT = 3, LAYOUT_QUADS = 4
+};
 
 static int repair_layout_override() {
     const char* s = getenv("CDCLQ_REPAIR_LAYOUT");
@@ -416,6 +419,7 @@ static int repair_layout_override() {
     if (!strcmp(s, "single")) return LAYOUT_SINGLE;
     if (!strcmp(s, "pairs")) return LAYOUT_PAIRS;
     if (!strcmp(s, "split")) return LAYOUT_SPLIT;
+    if (!strcmp(s, "quads")) return LAYOUT_QUADS;
     return LAYOUT_AUTO;
 }
 
@@ -932,6 +936,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
     size_t max_rows = 0;
     for (auto& P : plans) max_rows = std::max(max_rows, std::min(P.rc, P.d_out));
     const int layout = repair_layout_override();
+    int layout_used = 5;  // reported in the run profile (cdclq_run_profile.repair_layout)
     const bool persistent = layout == LAYOUT_AUTO ? total_chunks >= (size_t)sms : layout != LAYOUT_PASSES;
     if (cdcl && (rp.do_cd || rp.do_refit) && persistent) {
         int* counter = nullptr;
@@ -941,6 +946,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         // chunks of more than one row tile: a 2-CTA cluster per chunk
         bool cluster = max_rows > (size_t)bm && max_rows <= (size_t)bm * RP_MAX_TILES_PER_CHUNK;
         int split = 0, split_sms = 0;  // > 0: the first `split` chunks run apart (see below)
+        bool quads = false;            // ... as 4-CTA clusters (else as 2-CTA clusters)
         if (!cluster && bm == 128) {
             // Launch layouts, compared by their estimated makespan (chunk work ~ rows x n^2 per pass):
             //  S  one CTA per 128-row chunk, two CTAs per SM: the efficient GEMM shape, but a chunk's passes run
@@ -950,7 +956,9 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             //  H  the heaviest chunks (the widest layers, first in launch order) as 2-CTA clusters whose CTAs each
             //     own an SM (an 8-warp CTA alone runs ~1.3x faster than when it shares the SM), concurrently with
             //     a persistent launch of the other chunks on the remaining SMs.
-            constexpr double E64 = 0.79, ALONE = 1.3;
+            //  Q  as H, the heavy chunks (two 64-row tiles each) over 4-CTA clusters that also split every GEMM's
+            //     columns between two CTAs (QS: the measured speed-up of a chunk over its 2-CTA form).
+            constexpr double E64 = 0.79, ALONE = 1.3, QS = 1.5;
             std::vector<double> cw(total_chunks);
             double total_w = 0.0, max_w = 0.0;
             for (size_t i = 0; i < total_chunks; i++) {
@@ -967,26 +975,40 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             // heavy prefix: the chunks of the widest layers
             size_t nh = 0;
             while (nh < total_chunks && chunks_l[nh].n == chunks_l[0].n) nh++;
+            bool two_tiles = true;  // the 4-CTA form takes chunks of exactly two 64-row tiles
+            for (size_t i = 0; i < nh; i++) two_tiles = two_tiles && chunks_l[i].rows > 64 && chunks_l[i].rows <= 128;
             if (nh < total_chunks && max_w > total_w / slots) {
                 double wh = 0.0;
                 for (size_t i = 0; i < nh; i++) wh += cw[i];
                 const double wl = total_w - wh;
                 for (int s_h = 2; s_h < sms; s_h += 2) {
-                    if ((size_t)s_h > 2 * nh) break;
-                    const double th = std::max(max_w / (2.0 * E64 * ALONE), wh / (s_h * E64 * ALONE));
+                    if ((size_t)s_h > 4 * nh) break;
                     const double tl = wl / (2.0 * (sms - s_h));
-                    const double t = std::max(th, tl);
-                    if (t < best) {
-                        best = t;
-                        mode = 2;
-                        split = (int)nh;
-                        split_sms = s_h;
+                    if ((size_t)s_h <= 2 * nh) {
+                        const double th = std::max(max_w / (2.0 * E64 * ALONE), wh / (s_h * E64 * ALONE));
+                        const double t = std::max(th, tl);
+                        if (t < best) {
+                            best = t;
+                            mode = 2;
+                            split = (int)nh;
+                            split_sms = s_h;
+                        }
+                    }
+                    if (two_tiles && s_h % 4 == 0) {
+                        const double th = std::max(max_w / (2.0 * E64 * ALONE * QS), wh / (0.5 * s_h * E64 * ALONE * QS));
+                        const double t = std::max(th, tl);
+                        if (t < best) {
+                            best = t;
+                            mode = 3;
+                            split = (int)nh;
+                            split_sms = s_h;
+                        }
                     }
                 }
             }
             if (layout == LAYOUT_SINGLE) mode = 0;
             if (layout == LAYOUT_PAIRS) mode = 1;
-            if (layout == LAYOUT_SPLIT) {
+            if (layout == LAYOUT_SPLIT || (layout == LAYOUT_QUADS && !two_tiles)) {
                 if (nh < total_chunks) {  // the widest layers' chunks apart, each cluster CTA on its own SM
                     mode = 2;
                     split = (int)nh;
@@ -994,13 +1016,19 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
                 } else {
                     mode = 0;  // one width only: nothing to split off
                 }
+            } else if (layout == LAYOUT_QUADS) {
+                mode = 3;  // the widest layers' chunks as quads (all of them when there is one width only)
+                split = (int)nh;
+                split_sms = (int)std::max<size_t>(4, std::min<size_t>(4 * nh, (size_t)sms / 2)) & ~3;
             }
             if (mode == 1) {
                 bm = 64;
                 cluster = true;
             }
-            if (mode != 2) split = 0;
+            if (mode != 2 && mode != 3) split = 0;
+            quads = mode == 3;
         }
+        layout_used = split > 0 ? (quads ? 4 : 3) : cluster ? 2 : 1;
         if (split > 0) {
             // heavy chunks on `st` (one CTA per SM), the others on a second stream, joined on `st`
             int* counter_l = nullptr;
@@ -1018,8 +1046,10 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
                 cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
                 maxsm = (size_t)v;
             }
-            rc = launch_repair_cluster(chunks_dev, split, rp, g0, sbw0, 64, counter, st, split_sms, maxsm / 2 + 4096);
-            if (!rc)
+            rc = quads ? launch_repair_quad(chunks_dev, split, rp, g0, sbw0, counter, st, split_sms, maxsm / 2 + 4096)
+                       : launch_repair_cluster(chunks_dev, split, rp, g0, sbw0, 64, counter, st, split_sms,
+                                               maxsm / 2 + 4096);
+            if (!rc && split < (int)total_chunks)
                 rc = launch_repair_persistent(chunks_dev + split, (int)total_chunks - split, rp, g0, sbw0, 128,
                                               counter_l, ls, 2 * (sms - split_sms));
             cudaEventRecord(join, ls);
@@ -1034,6 +1064,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         repair_launches = 1;
         pev.record(4, st);
     } else if (cdcl && (rp.do_cd || rp.do_refit)) {
+        layout_used = 0;
         size_t max_passes = std::max<size_t>(cfg.passes, 1);
         for (size_t p = 0; p < max_passes; p++) {
             if ((rc = launch_repair_pass(chunks_dev, slices_dev, (int)slices.size(), acc_dev, rp, (int)plans[0].g,
@@ -1114,6 +1145,7 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
         pf.launches = g_launches.load() - launches0;
         pf.factor_batches = factor_batches;
         pf.ms_host = (now_s() - t_start) * 1e3;
+        pf.repair_layout = (uint64_t)layout_used;
     }
 
     // ---- statistics, summed over chunks in order (src/engine.rs:786-797)

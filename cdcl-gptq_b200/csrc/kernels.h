@@ -136,6 +136,10 @@ int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const Rep
 // smem_floor > 0 reserves that much shared memory per CTA so that no other CTA shares its SM.
 int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
                           int* counter_dev, cudaStream_t st, int max_ctas = 0, size_t smem_floor = 0);
+// A 4-CTA cluster per chunk of exactly two 64-row tiles: row tile x column half of every repair GEMM, one CTA per SM
+// (smem_floor reserves the SM).  max_ctas = the SMs given to the launch.
+int launch_repair_quad(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                       int* counter_dev, cudaStream_t st, int max_ctas, size_t smem_floor);
 
 // ---------------------------------------------------------------------------------------------------------
 // Generic f32 GEMM with the fixed order: C = alpha*A*B (+ beta*C), A row-major or transposed (gemm.cu)

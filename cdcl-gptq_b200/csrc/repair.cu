@@ -143,6 +143,14 @@ int launch_repair_cluster(const ChunkInfo* chunks_dev, int nchunks, const Repair
                      : launch_repair_cluster_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas);
 }
 
+int launch_repair_quad(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw,
+                       int* counter_dev, cudaStream_t st, int max_ctas, size_t smem_floor) {
+    if (nchunks == 0) return 0;
+    size_t smem = repair_smem_bytes(g, sbw, 64);
+    if (smem < smem_floor) smem = smem_floor;
+    return launch_repair_quad_bm64(chunks_dev, nchunks, rp, smem, counter_dev, st, max_ctas);
+}
+
 int launch_repair_persistent(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, int g, int sbw, int bm,
                              int* counter_dev, cudaStream_t st, int max_ctas) {
     if (nchunks == 0) return 0;

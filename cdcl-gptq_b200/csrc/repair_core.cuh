@@ -133,6 +133,46 @@ __device__ void gemm_to_tile(const AM& am, const float* b, int64_t ldb, int64_t 
     __syncthreads();
 }
 
+// Column split of the repair GEMMs between the two CTAs of a row tile in a 4-CTA cluster (cluster ranks 2 t + ch,
+// t the row tile, ch the column half): CTA ch computes half of a result tile's columns and writes them into its
+// partner's copy of the tile through distributed shared memory, so both hold the whole result; everything after
+// the GEMMs (the per-row refit, the coordinate sweeps) runs identically in both CTAs, but only ch = 0 writes
+// global memory (E, W_hat, codes, scales), and cluster barriers order those writes before the partner's next
+// reads.  Each element of a result keeps its single accumulation order, so results are those of one CTA.
+struct ColSplit {
+    int ch;       // -1: no split (the whole tile in this CTA); 0 / 1: the column half this CTA computes
+    int partner;  // cluster rank of the CTA holding the other half
+    __device__ __forceinline__ bool writes() const { return ch == 0; }
+};
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// gemm_to_tile, split by columns between the CTAs of a ColSplit pair (ends with the whole tile in both).
+template <int BM, bool SPLIT, class AM>
+__device__ void gemm_to_tile_cs(const AM& am, const float* b, int64_t ldb, int64_t col0, int wd, int K, float* out,
+                                int ldo, float* stage, const ColSplit& cs) {
+    if constexpr (!SPLIT) {
+        gemm_to_tile<BM>(am, b, ldb, col0, wd, K, out, ldo, stage);
+        return;
+    }
+    namespace cg = cooperative_groups;
+    const int h0 = min(wd, ((wd + 1) / 2 + 3) & ~3);  // columns of half 0
+    const int c_begin = cs.ch == 0 ? 0 : h0, c_count = cs.ch == 0 ? h0 : wd - h0;
+    cluster_sync_all();  // the partner's global writes before this GEMM (E rows) are visible
+    if (c_count > 0) gemm_to_tile<BM>(am, b, ldb, col0 + c_begin, c_count, K, out + (size_t)c_begin * ldo, ldo, stage);
+    cluster_sync_all();  // both halves computed; neither CTA still reads its staging area (inside `out`)
+    float* peer = cg::this_cluster().map_shared_rank(out, cs.partner);
+    constexpr int Q = BM / 4;
+    for (int idx = threadIdx.x; idx < c_count * Q; idx += blockDim.x) {
+        const int c = idx / Q, r4 = (idx - c * Q) * 4;
+        const size_t o = (size_t)(c_begin + c) * ldo + r4;
+        *reinterpret_cast<float4*>(peer + o) = *reinterpret_cast<const float4*>(out + o);
+    }
+    cluster_sync_all();  // the partner's half has arrived
+}
+
 // Tile staging between the row-major global matrices and the [col][row] shared-memory tiles.  A thread moves
 // one column of four consecutive rows: its global accesses are coalesced across the warp (consecutive
 // columns), and its shared-memory word lands in a distinct bank per column (strides CSLD / LDW).
@@ -271,9 +311,10 @@ __device__ __forceinline__ TileSmem tile_smem(unsigned char* raw, int g, int sbw
 // ---------------------------------------------------------------------------------------------------------
 // Closed-form scale refit of every (row, group) of the rows [r0, r0 + rs) of a chunk, groups in order
 // (src/engine.rs:534-589).  Thread r < rs accumulates its row's accepted loss deltas and refits.
-template <int BM>
+template <int BM, bool SPLIT = false>
 __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& sm, double& my_delta,
-                           unsigned long long& my_upd) {
+                           unsigned long long& my_upd, const ColSplit& split) {
+    const bool writer = !SPLIT || split.writes();  // the CTA that writes global memory
     constexpr int LD = RepairTiles<BM>::LD, CSLD = RepairTiles<BM>::CSLD;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng;
     float* E = ci.e + (int64_t)r0 * n;
@@ -288,13 +329,16 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         const int c0 = gi * g, wd = min(g, n - c0);
         stage_codes<BM>(cs, CODES, n, c0, rs, wd);
         if (tid < BM) sm.zrow[tid] = (tid < rs) ? ZR[(int64_t)tid * ng + gi] : 0.0f;
+        // the group's current scale, read before the GEMMs: with a column split the partner CTA writes the new
+        // scale once both have passed the GEMMs' cluster barriers
+        const float s_old = (tid < rs) ? SC[(int64_t)tid * ng + gi] : 0.0f;
         __syncthreads();
         // num = sum_k u_k * G_k with G = E H[:, c0:c1]
         float num = 0.0f, den = 0.0f;
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             tile, LD, tile);
+            gemm_to_tile_cs<BM, SPLIT>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                                tile, LD, tile, split);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
@@ -307,8 +351,8 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         // den = sum_k u_k * (u H_CC)_k
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            gemm_to_tile<BM>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
-                             wt, wd, tile, LD, tile);
+            gemm_to_tile_cs<BM, SPLIT>(AFromCodes{cs, sm.zrow, rs, wd}, H + (int64_t)c0 * n, (int64_t)n, (int64_t)(c0 + t0),
+                                wt, wd, tile, LD, tile, split);
             if (tid < rs) {
                 const float zr = sm.zrow[tid];
                 for (int k = 0; k < wt; k++) {
@@ -320,14 +364,13 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
         }
         if (tid < BM) sm.accept[tid] = 0;
         if (tid < rs && den > 1e-30f) {
-            const float s_old = SC[(int64_t)tid * ng + gi];
             float s_new = round_f16(__fadd_rn(s_old, __fdiv_rn(num, den)));
             if (!(s_new >= kF16MinNormal)) s_new = kF16MinNormal;  // f32::max(x, MIN)
             const float d = __fsub_rn(s_new, s_old);
             const float dlf = __fadd_rn(__fmul_rn(__fmul_rn(-2.0f, d), num), __fmul_rn(__fmul_rn(d, d), den));
             const double dl = (double)dlf;
             if (dl < 0.0) {
-                SC[(int64_t)tid * ng + gi] = s_new;
+                if (writer) SC[(int64_t)tid * ng + gi] = s_new;
                 sm.snew[tid] = s_new;
                 sm.accept[tid] = 1;
                 my_delta = __dadd_rn(my_delta, dl);
@@ -335,7 +378,7 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
             }
         }
         __syncthreads();
-        for (int idx = tid; idx < rs * wd; idx += blockDim.x) {
+        for (int idx = tid; idx < rs * wd && writer; idx += blockDim.x) {
             int rr = idx / wd, k = idx - rr * wd;
             if (sm.accept[rr]) {
                 float u = __fsub_rn((float)cs[k * CSLD + rr], sm.zrow[rr]);
@@ -350,9 +393,10 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
 }
 
 // Coordinate descent over the selected sub-blocks for rows [r0, r0 + rs) (src/engine.rs:600-658).
-template <int BM>
+template <int BM, bool SPLIT = false>
 __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
-                        unsigned long long& my_upd) {
+                        unsigned long long& my_upd, const ColSplit& split) {
+    const bool writer = !SPLIT || split.writes();  // the CTA that writes global memory
     constexpr int LD = RepairTiles<BM>::LDG, CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
     constexpr int P = RepairTiles<BM>::P;
     const int tid = threadIdx.x, n = ci.n, g = ci.g, ng = ci.ng, sbw = ci.sbw;
@@ -381,6 +425,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
     for (int si = 0; si < n_sel; si++) {
         const int s = ci.sel[si];
         const int c0 = s * sbw, wd = min(sbw, n - c0);
+        if (SPLIT) cluster_sync_all();  // the partner's codes / W_hat / E / scale writes are visible
         stage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         if (hss_full) {
             for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
@@ -392,8 +437,8 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         }
         for (int t0 = 0; t0 < wd; t0 += 128) {
             int wt = min(128, wd - t0);
-            gemm_to_tile<BM>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
-                             gt + (size_t)t0 * LD, LD, sm.cd_stage);
+            gemm_to_tile_cs<BM, SPLIT>(AFromE{E, (int64_t)n, rs, n, (n % 4 == 0)}, H, (int64_t)n, (int64_t)(c0 + t0), wt, n,
+                                gt + (size_t)t0 * LD, LD, sm.cd_stage, split);
         }
         if (r < rs) {
             // The P threads of a row take every decision together (identical inputs, identical results) and
@@ -448,8 +493,10 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                         if (h == 0) {
                             wqs[jj * LDW + r] = newdq;
                             cs[jj * CSLD + r] = qc;
-                            float* ep = &E[(int64_t)r * n + j];
-                            *ep = __fadd_rn(*ep, de);
+                            if (writer) {
+                                float* ep = &E[(int64_t)r * n + j];
+                                *ep = __fadd_rn(*ep, de);
+                            }
                             row_upd++;
                         }
                         changed = true;
@@ -464,7 +511,7 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
             }
         }
         __syncthreads();
-        unstage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
+        if (writer) unstage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         __syncthreads();
     }
     if (tid < BM) {
@@ -497,13 +544,14 @@ __device__ __forceinline__ void tile_reduce(int rs, const TileSmem& sm, double m
 
 // One tile of one pass (refit then coordinate descent, or the final refit alone); the tile's delta and
 // update count are valid in thread 0.
-template <int BM>
+template <int BM, bool SPLIT = false>
 __device__ __forceinline__ void run_tile(const ChunkInfo& ci, int r0, int rs, const RepairParams& rp, bool final_refit,
-                                         const TileSmem& sm, double& d, unsigned long long& u) {
+                                         const TileSmem& sm, double& d, unsigned long long& u,
+                                         const ColSplit& split = ColSplit{-1, 0}) {
     double my_delta = 0.0;
     unsigned long long my_upd = 0ull;
-    if (rp.do_refit) refit_tile<BM>(ci, r0, rs, sm, my_delta, my_upd);
-    if (rp.do_cd && !final_refit) cd_tile<BM>(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd);
+    if (rp.do_refit) refit_tile<BM, SPLIT>(ci, r0, rs, sm, my_delta, my_upd, split);
+    if (rp.do_cd && !final_refit) cd_tile<BM, SPLIT>(ci, r0, rs, rp.cd_sweeps, sm, my_delta, my_upd, split);
     tile_reduce<BM>(rs, sm, my_delta, my_upd, d, u);
 }
 
@@ -666,6 +714,73 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2)
 }
 
 
+// Mode Q - persistent 4-CTA clusters for chunks of exactly two row tiles: cluster rank 2 t + ch runs row tile t with
+// column half ch of every repair GEMM (ColSplit); the ch = 0 CTAs report their tile's partial sums to rank 0, which
+// applies the stop rule in tile order and writes the decision into the other three ranks.  The heaviest chunks
+// (the widest layers' rows, whose passes are the longest sequential chains of a rank's repair) get four SMs.
+template <int BM>
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256, 1)
+    repair_quad_kernel(const ChunkInfo* __restrict__ chunks, int nchunks, RepairParams rp, int* __restrict__ counter) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int s_chunk, s_done;
+    __shared__ ChunkInfo ci;
+    __shared__ double s_tile_delta[2];
+    __shared__ unsigned long long s_tile_upd[2];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int t = rank >> 1;  // row tile
+    const ColSplit split{rank & 1, rank ^ 1};
+    const int tid = threadIdx.x;
+    int* chunk0 = cluster.map_shared_rank(&s_chunk, 0);
+    double* tdelta0 = cluster.map_shared_rank(&s_tile_delta[0], 0);
+    unsigned long long* tupd0 = cluster.map_shared_rank(&s_tile_upd[0], 0);
+    for (;;) {
+        if (rank == 0 && tid == 0) s_chunk = atomicAdd(counter, 1);
+        cluster.sync();
+        const int c = *chunk0;
+        if (tid == 0 && c < nchunks) ci = chunks[c];
+        cluster.sync();  // every rank has read rank 0's s_chunk before anyone may leave or overwrite it
+        if (c >= nchunks) return;
+        ChunkState* st = ci.st;
+        const TileSmem sm = tile_smem<BM>(smem_raw, ci.g, ci.sbw);
+        if (tid == 0) s_done = st->done;
+        __syncthreads();
+        const int r0 = t * BM, rs = min(BM, ci.rows - r0);  // the host gives this kernel two-tile chunks only
+        for (int pass = 0; pass < rp.max_passes && !s_done; pass++) {
+            double d;
+            unsigned long long u;
+            run_tile<BM, true>(ci, r0, rs, rp, false, sm, d, u, split);
+            if (tid == 0 && split.ch == 0) {
+                tdelta0[t] = d;
+                tupd0[t] = u;
+            }
+            cluster.sync();  // both tiles' partials are in rank 0; every global write of the pass is visible
+            if (rank == 0 && tid == 0) {
+                apply_pass(st, __dadd_rn(__dadd_rn(0.0, s_tile_delta[0]), s_tile_delta[1]), s_tile_upd[0] + s_tile_upd[1],
+                           rp.tol);
+                for (int q = 0; q < 4; q++) *cluster.map_shared_rank(&s_done, q) = st->done;
+            }
+            cluster.sync();  // the decision is visible in every rank
+        }
+        if (rp.do_refit) {  // final refit (src/engine.rs:668-670)
+            double d;
+            unsigned long long u;
+            run_tile<BM, true>(ci, r0, rs, rp, true, sm, d, u, split);
+            if (tid == 0 && split.ch == 0) {
+                tdelta0[t] = d;
+                tupd0[t] = u;
+            }
+            cluster.sync();
+            if (rank == 0 && tid == 0) {
+                st->loss_delta = __dadd_rn(st->loss_delta, __dadd_rn(__dadd_rn(0.0, s_tile_delta[0]), s_tile_delta[1]));
+                st->updates += s_tile_upd[0] + s_tile_upd[1];
+            }
+        }
+        cluster.sync();  // the chunk's last global writes and rank 0's bookkeeping precede the next chunk
+    }
+}
+
 static inline int set_repair_smem(const void* fn, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     return e == cudaSuccess ? 0 : cuda_error(e, "repair smem attribute");
@@ -695,6 +810,20 @@ static int launch_cluster_bm(const ChunkInfo* chunks_dev, int nchunks, const Rep
     CDCLQ_LAUNCH(repair_cluster_kernel<BM>, 2 * clusters, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_error(e, "repair_cluster_kernel launch");
+}
+
+template <int BM>
+static int launch_quad_bm(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                          int* counter_dev, cudaStream_t st, int max_ctas) {
+    int rc = set_repair_smem((const void*)repair_quad_kernel<BM>, smem);
+    if (rc) return rc;
+    int quads = max_ctas / 4;
+    if (quads > nchunks) quads = nchunks;
+    if (quads < 1) quads = 1;
+    CDCLQ_CUDA_TRY(cudaMemsetAsync(counter_dev, 0, sizeof(int), st));
+    CDCLQ_LAUNCH(repair_quad_kernel<BM>, 4 * quads, 256, smem, st, chunks_dev, nchunks, rp, counter_dev);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_error(e, "repair_quad_kernel launch");
 }
 
 template <int BM>
@@ -734,6 +863,8 @@ int launch_repair_persistent_bm64(const ChunkInfo* chunks_dev, int nchunks, cons
                                   int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_cluster_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
                                int* counter_dev, cudaStream_t st, int max_ctas);
+int launch_repair_quad_bm64(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
+                            int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_persistent_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,
                                    int* counter_dev, cudaStream_t st, int max_ctas);
 int launch_repair_cluster_bm128(const ChunkInfo* chunks_dev, int nchunks, const RepairParams& rp, size_t smem,

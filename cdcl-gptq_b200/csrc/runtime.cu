@@ -187,9 +187,11 @@ int rt_group_end(Runtime* rt) {
     return nccl_settle(rt, nccl().GroupEnd(), "ncclGroupEnd");
 }
 
-int rt_broadcast(Runtime* rt, void* buf, size_t bytes, int root) {
+int rt_broadcast(Runtime* rt, void* buf, size_t bytes, int root) { return rt_broadcast_on(rt, rt->st, buf, bytes, root); }
+
+int rt_broadcast_on(Runtime* rt, cudaStream_t stream, void* buf, size_t bytes, int root) {
     if (rt->nranks == 1 || bytes == 0) return 0;
-    ncclResult_t r = nccl().Broadcast(buf, buf, bytes, ncclUint8, root, (ncclComm_t)rt->comm, rt->st);
+    ncclResult_t r = nccl().Broadcast(buf, buf, bytes, ncclUint8, root, (ncclComm_t)rt->comm, stream);
     return r == ncclSuccess || r == ncclInProgress ? 0 : nccl_error(rt, r, "ncclBroadcast");
 }
 
@@ -433,7 +435,16 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
     std::vector<std::vector<uint32_t>> perm(nly);
     std::vector<std::vector<uint8_t>> gbits(nly);
     std::vector<size_t> nskel(nly, 0);
+    std::vector<long> first_of_input(nin, -1);  // without a skeleton every layer of an input shares its permutation
     for (size_t l = 0; l < nly && !rc; l++) {
+        const long f = first_of_input[ly[l].input];
+        if (!skel && f >= 0) {
+            perm[l] = perm[f];
+            gbits[l] = gbits[f];
+            nskel[l] = nskel[f];
+            continue;
+        }
+        first_of_input[ly[l].input] = (long)l;
         std::vector<double> cs;
         if (skel) {
             cs.resize(part[l].n);
@@ -491,31 +502,53 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
                                              uo.data(), 1, st);
     }
     if ((rc = rt_agree(rt, rc))) return rc;
+    // The factors travel on the communication stream, ordered after this rank's factorisations; meanwhile the
+    // layers whose factor this rank computed itself (wave A) are quantized on the work stream, and the other
+    // layers (wave B) once every factor has landed.  With a skeleton the factors are per layer: one wave.
+    cudaEvent_t ev_f = nullptr, ev_b = nullptr;
+    CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_f, cudaEventDisableTiming));
+    CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_b, cudaEventDisableTiming));
+    struct Ev {
+        cudaEvent_t a, b;
+        ~Ev() {
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+        }
+    } evs{ev_f, ev_b};
+    CDCLQ_CUDA_TRY(cudaEventRecord(ev_f, st));
+    CDCLQ_CUDA_TRY(cudaStreamWaitEvent(rt->comm_st, ev_f, 0));
     if ((rc = rt_group_begin(rt))) return rc;
     if (!skel) {
-        for (size_t i = 0; i < nin && !rc; i++) rc = rt_broadcast(rt, u[i], ns[i] * ns[i] * sizeof(float), owner[i]);
+        for (size_t i = 0; i < nin && !rc; i++)
+            rc = rt_broadcast_on(rt, rt->comm_st, u[i], ns[i] * ns[i] * sizeof(float), owner[i]);
     } else {
         for (size_t l = 0; l < nly && !rc; l++)
-            rc = rt_broadcast(rt, part[l].u, part[l].n * part[l].n * sizeof(float), lowner[l]);
+            rc = rt_broadcast_on(rt, rt->comm_st, part[l].u, part[l].n * part[l].n * sizeof(float), lowner[l]);
     }
     {
         int r2 = rt_group_end(rt);
         if (rc || r2) return rc ? rc : r2;
     }
+    CDCLQ_CUDA_TRY(cudaEventRecord(ev_b, rt->comm_st));
 
-    // ---- this rank's rows, one batch per row chunk (layers whose automatic row chunk differs)
+    // ---- this rank's rows, one batch per wave and row chunk (layers whose automatic row chunk differs)
     std::vector<cdclq_layer_stats> lst(nly);
     std::vector<std::vector<uint32_t>> scratch_perm(nly);
     std::vector<std::vector<uint8_t>> scratch_gb(nly);
-    std::map<size_t, std::vector<size_t>> by_rc;
+    std::map<std::pair<int, size_t>, std::vector<size_t>> by_rc;  // (wave, row chunk) -> layers
     for (size_t l = 0; l < nly; l++)
-        if (part[l].r1 > part[l].r0) by_rc[part[l].rc].push_back(l);
+        if (part[l].r1 > part[l].r0) by_rc[{(!skel && owner[ly[l].input] == me) ? 0 : 1, part[l].rc}].push_back(l);
     std::vector<cdclq_batch_input> in_dev(nin);
     for (size_t i = 0; i < nin; i++) in_dev[i] = cdclq_batch_input{hdev[i], ns[i]};
+    bool waited = false;
     for (auto& kv : by_rc) {
         if (rc) break;
+        if (kv.first.first == 1 && !waited) {
+            CDCLQ_CUDA_TRY(cudaStreamWaitEvent(st, ev_b, 0));
+            waited = true;
+        }
         cdclq_config c = cfg;
-        c.row_chunk = kv.first;
+        c.row_chunk = kv.first.second;
         std::vector<cdclq_batch_layer> d(kv.second.size());
         for (size_t k = 0; k < kv.second.size(); k++) {
             const size_t l = kv.second[k];
@@ -539,6 +572,10 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
         }
         rc = skel ? cdclq_quantize_batch(in_dev.data(), nin, d.data(), d.size(), &c, 1, st)
                   : cdclq_quantize_batch_prepared(in_dev.data(), nin, u.data(), d.data(), d.size(), &c, 1, st);
+    }
+    if (!waited) {  // no wave B rows here: the factors still land before this call returns
+        cudaError_t e = cudaStreamWaitEvent(st, ev_b, 0);
+        if (!rc && e != cudaSuccess) rc = cuda_error(e, "factor broadcast wait");
     }
     if ((rc = rt_agree(rt, rc))) return rc;
 
@@ -698,6 +735,7 @@ int cdclq_runtime_create(int device, int nranks, int rank, const uint8_t* unique
     rt->timeout_s = timeout_s > 0.0 ? timeout_s : 600.0;
     e = cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking);
     rt->owned_stream = e == cudaSuccess;
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&rt->comm_st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&rt->flag_dev, 2 * sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMalloc(&rt->msg_dev, 512);
     if (e != cudaSuccess) rc = cuda_error(e, "runtime set-up");
@@ -745,9 +783,11 @@ void cdclq_runtime_destroy(cdclq_runtime* rt) {
         }
     }
     if (rt->st) cudaStreamSynchronize(rt->st);
+    if (rt->comm_st) cudaStreamSynchronize(rt->comm_st);
     cudaFree(rt->flag_dev);
     cudaFree(rt->msg_dev);
     if (rt->owned_stream && rt->st) cudaStreamDestroy(rt->st);
+    if (rt->comm_st) cudaStreamDestroy(rt->comm_st);
     delete rt;
 }
 

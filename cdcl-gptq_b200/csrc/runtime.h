@@ -19,6 +19,7 @@ struct Runtime {
     int rank = 0;
     double timeout_s = 600.0;
     cudaStream_t st = nullptr;
+    cudaStream_t comm_st = nullptr;  // collectives that overlap work on st (the factor broadcasts)
     void* comm = nullptr;      // ncclComm_t
     bool broken = false;       // a collective failed or timed out: the communicator was aborted
     int32_t* flag_dev = nullptr;  // 2 ints: error consensus
@@ -38,6 +39,7 @@ std::vector<int> assign_owners(const std::vector<size_t>& ns, int nranks, int po
 int rt_group_begin(Runtime* rt);
 int rt_group_end(Runtime* rt);
 int rt_broadcast(Runtime* rt, void* buf, size_t bytes, int root);
+int rt_broadcast_on(Runtime* rt, cudaStream_t stream, void* buf, size_t bytes, int root);
 int rt_send(Runtime* rt, const void* buf, size_t bytes, int peer);
 int rt_recv(Runtime* rt, void* buf, size_t bytes, int peer);
 int rt_allreduce_sum_f64(Runtime* rt, double* buf_dev, size_t count);

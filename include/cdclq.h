@@ -374,6 +374,9 @@ typedef struct cdclq_run_profile {
     uint64_t launches;      /* kernel launches issued by the call */
     uint64_t factor_batches; /* factorisation launch batches: one per width when all fit in free memory */
     double ms_host;         /* host wall time of the call */
+    uint64_t repair_layout; /* 0 one launch per pass, 1 persistent CTAs, 2 persistent 2-CTA clusters, 3 heavy chunks
+                               as SM-owning 2-CTA clusters beside a persistent launch, 4 the same as 4-CTA clusters
+                               with column-split GEMMs, 5 none (GPTQ only) */
 } cdclq_run_profile;
 
 int cdclq_last_run_profile(cdclq_run_profile* out);

@@ -9,8 +9,9 @@ passes every row chunk executed and the accepted moves identical.
 
 Each case runs under every repair launch layout the engine can choose for a model (CDCLQ_REPAIR_LAYOUT): one
 launch per pass over 64-row slices (what a single layer gets), the persistent kernel with one 128-row CTA per
-chunk (what configs[1] gets on one GPU), and 2-CTA clusters of 64-row tiles (what a rank's shard gets on
-several GPUs); the batch test below adds the heavy/light split.  The wide widths exercise what the small
+chunk (what configs[1] gets on one GPU), 2-CTA clusters of 64-row tiles (what a rank's shard gets on several
+GPUs), and 4-CTA clusters that also split every GEMM's columns between two CTAs (the heaviest chunks of a shard
+on several GPUs); the batch test below adds the heavy/light split in both cluster forms.  The wide widths exercise what the small
 cases cannot: the repair's K loops over 5632 to 28672 columns, act-order and skeleton permutations of wide
 Hessians, the factorisation of 11008- to 28672-wide inputs.
 """
@@ -30,7 +31,7 @@ pytestmark = pytest.mark.gpu
 with open(os.path.join(GOLDEN, "wide_cases.json")) as _f:
     FIXTURE = json.load(_f)
 NAMES = sorted(FIXTURE, key=lambda k: (FIXTURE[k]["n"], k))
-LAYOUTS = ("passes", "single", "pairs")
+LAYOUTS = ("passes", "single", "pairs", "quads")
 _H = {}
 
 
@@ -132,7 +133,7 @@ def test_wide_batch_heavy_split(gpu, monkeypatch):
     _, h_light = orc.problem(1, 256, 600, 501)  # 256 wide: the same effective group (128) as the heavy layer
     w_light = orc.rng_normal(502, 38400 * 256, 0.02).reshape(38400, 256)
     qb, sb = orc.quantize_layer(w_light, 38400, 256, h_light, None, "light", cfg)
-    for layout in ("", "split"):
+    for layout in ("", "split", "quads"):
         monkeypatch.setenv("CDCLQ_REPAIR_LAYOUT", layout)
         outs, stats = _batch([h_heavy, np.ascontiguousarray(h_light)], [(0, w_heavy), (1, w_light)], cfg)
         o = outs[0]
