@@ -428,10 +428,10 @@ def run_reference_arm(args, torch, rank, world):
 
 
 def repair_traffic_bytes(weights):
-    """DRAM bytes of one repair launch for `weights` weights, from the committed ncu summary of the repair
-    kernel (dram__bytes_read.sum + dram__bytes_write.sum of the full launch, per weight); None when the
+    """DRAM bytes of one repair launch for `weights` weights, from the committed ncu summary of the repair kernel
+    on the 2-layer case (dram__bytes_read.sum + dram__bytes_write.sum of the launch, per weight); None when the
     summary is absent."""
-    path = os.path.join(ROOT, "profiles", "repair_persistent_kernel_tinyllama_22layers.md")
+    path = os.path.join(ROOT, "profiles", "repair_persistent_kernel_tinyllama_2layers.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_weight:"):
@@ -1061,7 +1061,8 @@ def main():
                 "bound": "fp32", "achieved": rep_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": rep_tflops / fp32_peak if fp32_peak else None,
                 "traffic": repair_traffic_bytes(prof["weights"]),
-                "traffic_source": "profiles/repair_persistent_kernel_tinyllama_22layers.md (ncu DRAM bytes of the full launch, per weight)",
+                "traffic_source": "profiles/repair_persistent_kernel_tinyllama_2layers.md (ncu DRAM bytes of the 2-layer "
+                                  "launch per weight, times this launch's weights)",
                 "peak_source": "measured in this run: cuBLAS SGEMM 8192^3 with TF32 off (FFMA); MEASURED_PEAKS.json "
                                "has no FP32 CUDA-core figure",
             },

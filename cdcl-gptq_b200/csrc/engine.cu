@@ -957,8 +957,9 @@ static int run(const std::vector<InputReq>& inputs, const std::vector<LayerReq>&
             //     own an SM (an 8-warp CTA alone runs ~1.3x faster than when it shares the SM), concurrently with
             //     a persistent launch of the other chunks on the remaining SMs.
             //  Q  as H, the heavy chunks (two 64-row tiles each) over 4-CTA clusters that also split every GEMM's
-            //     columns between two CTAs (QS: the measured speed-up of a chunk over its 2-CTA form).
-            constexpr double E64 = 0.79, ALONE = 1.3, QS = 1.5;
+            //     columns between two CTAs (QS: the measured speed-up of a 5632-wide chunk over its 2-CTA form:
+            //     only the GEMMs shrink, the per-row sequential refit and sweeps keep their latency).
+            constexpr double E64 = 0.79, ALONE = 1.3, QS = 1.2;
             std::vector<double> cw(total_chunks);
             double total_w = 0.0, max_w = 0.0;
             for (size_t i = 0; i < total_chunks; i++) {
