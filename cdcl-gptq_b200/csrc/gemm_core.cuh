@@ -5,7 +5,9 @@
 // rounding decisions (code choice, scale acceptance).  A tensor-core f32 emulation (3xTF32 / bf16x9) rounds
 // differently and would turn exact parity into tie-level agreement.  This core keeps, for every output
 // element, one f32 accumulator that receives the products in increasing k through __fmaf_rn, starting from
-// +0 - the fixed order of the oracle - so results are bit-identical to it.
+// +0 - the fixed order of the oracle - so results are bit-identical to it.  The products are issued as packed
+// f32x2 FMAs (`fma.rn.f32x2`, two lanes of the accumulator tile per instruction): each lane is an independent
+// IEEE round-to-nearest FMA, so packing changes the instruction count, not a single rounding.
 //
 // CTA tile BM x BN (BM in {64, 128} rows, BN in {32, 64, 128} columns), 256 threads in a 16 x 16 grid, so a
 // thread owns TM = BM/16 rows x TN = BN/16 columns: rows ty*TM .. ty*TM+TM-1 and columns in TN/4 groups of 4,
@@ -84,6 +86,19 @@ __device__ __forceinline__ void frag_load(float (&av)[S::TM], float (&bv)[S::TN]
     }
 }
 
+// (c0, c1) += (a0 * b0, a1 * b1) as one packed f32x2 FMA: two independent IEEE round-to-nearest FMAs, each the
+// same result as __fmaf_rn on its lane, so the per-element accumulation order is unchanged.
+__device__ __forceinline__ void ffma2(float& c0, float& c1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ta, tb, tc;\n\t"
+        "mov.b64 ta, {%2, %3};\n\t"
+        "mov.b64 tb, {%4, %5};\n\t"
+        "mov.b64 tc, {%0, %1};\n\t"
+        "fma.rn.f32x2 tc, ta, tb, tc;\n\t"
+        "mov.b64 {%0, %1}, tc;\n\t}"
+        : "+f"(c0), "+f"(c1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // SWZ: the A stage was written with the k-dependent row swizzle (staged operands); resident A is not swizzled.
 template <class S, bool SWZ>
 __device__ __forceinline__ void gemm_stage_mac(float (&acc)[S::TM][S::TN], const float* __restrict__ As,
@@ -95,10 +110,12 @@ __device__ __forceinline__ void gemm_stage_mac(float (&acc)[S::TM][S::TN], const
         if (kk + 1 < S::KT && kk + 1 < kn)
             frag_load<S, SWZ>(av[(kk + 1) & 1], bv[(kk + 1) & 1], As, Bs, kk + 1, ty, tx);
         if (kk < kn) {
+            // Packed f32x2 FMAs (sm_100): half the FMA instructions of a scalar loop, same per-element order.
 #pragma unroll
             for (int i = 0; i < S::TM; i++)
 #pragma unroll
-                for (int j = 0; j < S::TN; j++) acc[i][j] = __fmaf_rn(av[kk & 1][i], bv[kk & 1][j], acc[i][j]);
+                for (int j = 0; j < S::TN; j += 2)
+                    ffma2(acc[i][j], acc[i][j + 1], av[kk & 1][i], av[kk & 1][i], bv[kk & 1][j], bv[kk & 1][j + 1]);
         }
     }
 }
