@@ -54,6 +54,23 @@ __device__ __forceinline__ void grid_mk(float lo, float hi, float maxq, float& s
     z = zero;
 }
 
+// A sufficient, division-free condition for a coordinate-descent step to keep a weight's code
+// (src/engine.rs:624-633: target = cur + g / h, q = clamp(round(target / s) + z, 0, maxq), a move iff
+// q != code).  Let m = code - z: small integers, so exact (zero points are integers; checked).  When
+// cur = RN(s * m) - checked through the FMA residual |s * m - cur| <= 2^-23 |cur| - the exact evaluation
+// t2 = RN(RN(cur + RN(g / h)) / s) satisfies |t2 - m| <= |g| / (h s) (1 + 3u) + 4.1u |m|, u = 2^-24, and
+// |m| <= 255 (8-bit codes) makes the last term < 6.3e-5.  So |g| < 0.4998 h s (evaluated in f32, two more
+// roundings of < 1.2e-7 relative) bounds |t2 - m| below 0.4999 + 6.3e-5 < 0.5: round(t2) = m, q = m + z =
+// code, and the step keeps the code.  Infinite or NaN operands and h <= 0 fail the test (the caller then
+// evaluates the step exactly).  The test never holds for a step that moves, so skipping the exact evaluation
+// when it holds changes no decision.
+__device__ __forceinline__ bool cd_keeps_code(float g, float h, float cur, float s, float m) {
+    const float lim = __fmul_rn(__fmul_rn(0.4998f, h), s);
+    const float res = __fmaf_rn(s, m, -cur);
+    return h > 0.0f && lim < INFINITY && fabsf(g) < lim && fabsf(res) <= __fmul_rn(fabsf(cur), 1.1920929e-7f) &&
+           m == rintf(m);
+}
+
 // The MSE clip ratio p_i = 1 - 0.02 * i (src/quant.rs:68-69), in f32.
 __device__ __forceinline__ float clip_ratio(int i) { return __fsub_rn(1.0f, __fmul_rn(0.02f, (float)i)); }
 

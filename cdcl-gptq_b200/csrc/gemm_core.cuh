@@ -111,11 +111,23 @@ __device__ __forceinline__ void gemm_stage_mac(float (&acc)[S::TM][S::TN], const
             frag_load<S, SWZ>(av[(kk + 1) & 1], bv[(kk + 1) & 1], As, Bs, kk + 1, ty, tx);
         if (kk < kn) {
             // Packed f32x2 FMAs (sm_100): half the FMA instructions of a scalar loop, same per-element order.
+            // Lanes pair along the longer side of the thread's tile, so the operand that must be duplicated
+            // into both lanes is the shorter fragment.
+            if constexpr (S::TM > S::TN) {
 #pragma unroll
-            for (int i = 0; i < S::TM; i++)
+                for (int j = 0; j < S::TN; j++)
 #pragma unroll
-                for (int j = 0; j < S::TN; j += 2)
-                    ffma2(acc[i][j], acc[i][j + 1], av[kk & 1][i], av[kk & 1][i], bv[kk & 1][j], bv[kk & 1][j + 1]);
+                    for (int i = 0; i < S::TM; i += 2)
+                        ffma2(acc[i][j], acc[i + 1][j], av[kk & 1][i], av[kk & 1][i + 1], bv[kk & 1][j],
+                              bv[kk & 1][j]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < S::TM; i++)
+#pragma unroll
+                    for (int j = 0; j < S::TN; j += 2)
+                        ffma2(acc[i][j], acc[i][j + 1], av[kk & 1][i], av[kk & 1][i], bv[kk & 1][j],
+                              bv[kk & 1][j + 1]);
+            }
         }
     }
 }

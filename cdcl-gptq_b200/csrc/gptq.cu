@@ -6,10 +6,13 @@
 //   2. columns are processed in order.  Four threads share a row: they compute the group grid together at a
 //      group start (min/max split four ways, the 24 MSE clip candidates split four ways), quantize the
 //      column redundantly, and split the rank-1 in-block compensation w1[:, j+1:i2] -= eps * U[j, j+1:i2]
-//      four ways.  The four lanes sit in one warp, so a __syncwarp orders consecutive columns.  The rows of U
-//      the compensation reads come from a shared-memory window of P1_UWIN rows, double-buffered with cp.async
-//      (the next window is in flight while the current one is used), so no global load sits inside the
-//      column-to-column dependency chain;
+//      four ways.  The four lanes sit in one warp, so a __syncwarp orders consecutive columns.  Columns go in
+//      micro-blocks of up to 8: a column's compensation of the rest of its micro-block is on the sequential
+//      chain, its compensation of the later columns is applied once per micro-block, every element taking
+//      the micro-block's terms in column order (the reference's sequence of roundings, fewer round trips).
+//      The rows of U the compensation reads come from a shared-memory window of P1_UWIN rows, double-buffered
+//      with cp.async (the next window is in flight while the current one is used), so no global load sits
+//      inside the column-to-column dependency chain;
 //   3. the deferred compensation w[:, i2:] -= err1 * U[i1:i2, i2:] runs on the FP32 GEMM core
 //      (A = err1 from shared memory, B = U tiles), one subtraction per element per block as in the reference.
 // Outputs per element: code, dequantized value, and eps^2 (consumed by the per-chunk conflict statistics).
@@ -32,6 +35,7 @@ static __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~
 // U window: up to P1_UWIN rows of U[j, i1:i1+B] per buffer, two buffers in the lazy GEMM's B staging area
 // (unused during the column loop): 2 * 16 * 128 floats = the Tile's B_STAGE_FLOATS; wider blocks get fewer rows.
 constexpr int P1_UWIN = 16;
+constexpr int P1_MB = 8;  // micro-block width of the column loop
 static_assert(2 * P1_UWIN * 128 <= P1Tile::B_STAGE_FLOATS, "the U window must fit the staging buffer");
 __host__ __device__ inline int p1_uwin(int B) {
     int w = (P1Tile::B_STAGE_FLOATS / 2) / B;
@@ -100,111 +104,136 @@ __global__ void __launch_bounds__(256, 2) gptq_phase1_kernel(const P1Item* __res
         const int uw = p1_uwin(B);
         load_u_window(stage, U, n, i1, i1, min(uw, cnt), cnt, B, uvec, tid);
 
-        for (int i = 0; i < cnt; i++) {
-            const int j = i1 + i;
-            if (i % uw == 0) {
-                // window i / uw has landed; every warp is done with the previous one, whose buffer now receives
+        // Micro-blocks of up to P1_MB columns inside one U window and one quantization group: the per-column
+        // chain quantizes a column and compensates only the rest of its micro-block; the columns past the
+        // micro-block then receive the micro-block's compensations in one pass, each element still taking
+        // them one at a time in column order (w -= e_i * U[i][k], i ascending): the reference's roundings.
+        for (int i0 = 0; i0 < cnt;) {
+            const int j0 = i1 + i0;
+            if (i0 % uw == 0) {
+                // window i0 / uw has landed; every warp is done with the previous one, whose buffer now receives
                 // the next window
                 if (uvec) cp_async_wait_all();
                 __syncthreads();
-                const int nw = i + uw;
+                const int nw = i0 + uw;
                 if (nw < cnt)
                     load_u_window(stage + ((nw / uw) & 1) * uw * B, U, n, i1, i1 + nw, min(uw, cnt - nw), cnt, B, uvec,
                                   tid);
             }
-            if (j % g == 0) {
-                // ---- group grid from the weights current at its first column (src/engine.rs:410-423)
-                const int gi = j / g, gend = min(j + g, n);
-                const uint32_t bits = it.gbits[gi];
-                maxq = (float)((1u << bits) - 1u);
-                float xmin = 0.0f, xmax = 0.0f;
-                for (int col = j + sub; col < gend; col += 4) {
-                    float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r] : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
-                    xmin = min_sel(xmin, v);
-                    xmax = max_sel(xmax, v);
-                }
+            // micro-block [i0, ie): ends at P1_MB columns, the window's end, the block's end or the next group
+            const int ie = min(min(i0 + P1_MB, cnt), min((i0 / uw + 1) * uw, g - j0 % g + i0));
+            float emb[P1_MB];
 #pragma unroll
-                for (int o = 1; o < 4; o <<= 1) {
-                    xmin = min_sel(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
-                    xmax = max_sel(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
-                }
-                if (xmin == 0.0f && xmax == 0.0f) {
-                    xmin = -1.0f;
-                    xmax = 1.0f;
-                }
-                grid_mk(xmin, xmax, maxq, s, z);
-                if (mse) {
-                    // this thread's 6 of the 24 clip candidates (ci = sub + 4m), each error summed over the
-                    // group's columns in order; one read of each value feeds all six
-                    constexpr int NC = 24 / 4;
-                    float cs[NC], cz[NC], cerr[NC];
-#pragma unroll
-                    for (int m = 0; m < NC; m++) {
-                        const float p = clip_ratio(sub + 4 * m);
-                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, cs[m], cz[m]);
-                        cerr[m] = 0.0f;
+            for (int m = 0; m < P1_MB; m++) {
+                const int i = i0 + m;
+                if (i >= ie) break;
+                const int j = i1 + i;
+                if (j % g == 0) {
+                    // ---- group grid from the weights current at its first column (src/engine.rs:410-423)
+                    const int gi = j / g, gend = min(j + g, n);
+                    const uint32_t bits = it.gbits[gi];
+                    maxq = (float)((1u << bits) - 1u);
+                    float xmin = 0.0f, xmax = 0.0f;
+                    for (int col = j + sub; col < gend; col += 4) {
+                        float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r] : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+                        xmin = min_sel(xmin, v);
+                        xmax = max_sel(xmax, v);
                     }
-                    for (int col = j; col < gend; col++) {
-                        const float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r]
-                                                   : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
-#pragma unroll
-                        for (int m = 0; m < NC; m++) {
-                            uint8_t c;
-                            float d;
-                            quant_code(v, cs[m], cz[m], maxq, c, d);
-                            const float e = __fsub_rn(d, v);
-                            cerr[m] = __fadd_rn(cerr[m], __fmul_rn(e, e));
-                        }
-                    }
-                    float best_err = INFINITY;
-                    int best_i = 24;
-#pragma unroll
-                    for (int m = 0; m < NC; m++) {
-                        if (cerr[m] < best_err) {
-                            best_err = cerr[m];
-                            best_i = sub + 4 * m;
-                        }
-                    }
-                    // first index of the strict minimum == min error, ties to the smaller index
 #pragma unroll
                     for (int o = 1; o < 4; o <<= 1) {
-                        float oe = __shfl_xor_sync(0xffffffffu, best_err, o);
-                        int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-                        if (oe < best_err || (oe == best_err && oi < best_i)) {
-                            best_err = oe;
-                            best_i = oi;
+                        xmin = min_sel(xmin, __shfl_xor_sync(0xffffffffu, xmin, o));
+                        xmax = max_sel(xmax, __shfl_xor_sync(0xffffffffu, xmax, o));
+                    }
+                    if (xmin == 0.0f && xmax == 0.0f) {
+                        xmin = -1.0f;
+                        xmax = 1.0f;
+                    }
+                    grid_mk(xmin, xmax, maxq, s, z);
+                    if (mse) {
+                        // this thread's 6 of the 24 clip candidates (ci = sub + 4m), each error summed over the
+                        // group's columns in order; one read of each value feeds all six
+                        constexpr int NC = 24 / 4;
+                        float cs[NC], cz[NC], cerr[NC];
+#pragma unroll
+                        for (int m = 0; m < NC; m++) {
+                            const float p = clip_ratio(sub + 4 * m);
+                            grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, cs[m], cz[m]);
+                            cerr[m] = 0.0f;
+                        }
+                        for (int col = j; col < gend; col++) {
+                            const float v = (col < i2) ? w1[(col - i1) * P1_W1LD + r]
+                                                       : (rvalid ? w[(int64_t)r * n + col] : 0.0f);
+#pragma unroll
+                            for (int m = 0; m < NC; m++) {
+                                uint8_t c;
+                                float d;
+                                quant_code(v, cs[m], cz[m], maxq, c, d);
+                                const float e = __fsub_rn(d, v);
+                                cerr[m] = __fadd_rn(cerr[m], __fmul_rn(e, e));
+                            }
+                        }
+                        float best_err = INFINITY;
+                        int best_i = 24;
+#pragma unroll
+                        for (int m = 0; m < NC; m++) {
+                            if (cerr[m] < best_err) {
+                                best_err = cerr[m];
+                                best_i = sub + 4 * m;
+                            }
+                        }
+                        // first index of the strict minimum == min error, ties to the smaller index
+#pragma unroll
+                        for (int o = 1; o < 4; o <<= 1) {
+                            float oe = __shfl_xor_sync(0xffffffffu, best_err, o);
+                            int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+                            if (oe < best_err || (oe == best_err && oi < best_i)) {
+                                best_err = oe;
+                                best_i = oi;
+                            }
+                        }
+                        if (best_i < 24) {
+                            float p = clip_ratio(best_i);
+                            grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, s, z);
                         }
                     }
-                    if (best_i < 24) {
-                        float p = clip_ratio(best_i);
-                        grid_mk(__fmul_rn(p, xmin), __fmul_rn(p, xmax), maxq, s, z);
+                    if (sub == 0 && rvalid) {
+                        int64_t so = (int64_t)(it.row0 + r) * ng + gi;
+                        it.scales[so] = s;
+                        it.zeros[so] = z;
                     }
                 }
-                if (sub == 0 && rvalid) {
-                    int64_t so = (int64_t)(it.row0 + r) * ng + gi;
-                    it.scales[so] = s;
-                    it.zeros[so] = z;
+                // ---- quantize column j and compensate the rest of the micro-block (src/engine.rs:424-448)
+                const float wv = w1[i * P1_W1LD + r];
+                uint8_t c;
+                float dq;
+                quant_code(wv, s, z, maxq, c, dq);
+                const float e = __fmul_rn(__fsub_rn(wv, dq), invd[i]);
+                emb[m] = e;
+                __syncwarp();
+                if (sub == 0) {
+                    err1[i * P1_ELD + r] = e;
+                    cbuf[i * P1_ROWS + r] = c;
+                    w1[i * P1_W1LD + r] = dq;  // column i is final: keep its dequantized value
                 }
+                const float* urow = stage + ((i / uw) & 1) * uw * B + (i % uw) * B;  // U[j, i1:i2]
+                for (int k = i + 1 + sub; k < ie; k += 4) {
+                    float* x = &w1[k * P1_W1LD + r];
+                    *x = __fsub_rn(*x, __fmul_rn(e, urow[k]));
+                }
+                __syncwarp();
             }
-            // ---- quantize column j and compensate the rest of the block (src/engine.rs:424-448)
-            const float wv = w1[i * P1_W1LD + r];
-            uint8_t c;
-            float dq;
-            quant_code(wv, s, z, maxq, c, dq);
-            const float inv_d = invd[i];
-            const float e = __fmul_rn(__fsub_rn(wv, dq), inv_d);
-            __syncwarp();
-            if (sub == 0) {
-                err1[i * P1_ELD + r] = e;
-                cbuf[i * P1_ROWS + r] = c;
-                w1[i * P1_W1LD + r] = dq;  // column i is final: keep its dequantized value
-            }
-            const float* urow = stage + ((i / uw) & 1) * uw * B + (i % uw) * B;  // U[j, i1:i2]
-            for (int k = i + 1 + sub; k < cnt; k += 4) {
-                float* x = &w1[k * P1_W1LD + r];
-                *x = __fsub_rn(*x, __fmul_rn(e, urow[k]));
+            // ---- the micro-block's compensations of the block's later columns, in column order per element
+            const int mb = ie - i0;
+            const float* ubase = stage + ((i0 / uw) & 1) * uw * B + (i0 % uw) * B;  // U[j0 + m, i1:i2] at m * B
+            for (int k = ie + sub; k < cnt; k += 4) {
+                float x = w1[k * P1_W1LD + r];
+#pragma unroll
+                for (int m = 0; m < P1_MB; m++)
+                    if (m < mb) x = __fsub_rn(x, __fmul_rn(emb[m], ubase[m * B + k]));
+                w1[k * P1_W1LD + r] = x;
             }
             __syncwarp();
+            i0 = ie;
         }
         __syncthreads();
 

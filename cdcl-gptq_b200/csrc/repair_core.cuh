@@ -392,6 +392,28 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
     }
 }
 
+// The rank-1 gradient update of one move, g[kk] += de * h(kk) for the columns kk = h0, h0 + P, ... < wd of one
+// row (the thread's share): eight columns at a time, all loads issued before the stores, so a move costs a few
+// shared-memory round trips instead of one per column.  Each element still receives one f32 multiply and add.
+template <int P, int LD, class HF>
+__device__ __forceinline__ void rank1_update(float* gt, int r, int h0, int wd, float de, HF hval) {
+    constexpr int U = 8;
+    for (int base = h0; base < wd; base += U * P) {
+        float hv[U], gv[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int kk = base + u * P;
+            hv[u] = kk < wd ? hval(kk) : 0.0f;
+            gv[u] = kk < wd ? gt[kk * LD + r] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int kk = base + u * P;
+            if (kk < wd) gt[kk * LD + r] = __fadd_rn(gv[u], __fmul_rn(de, hv[u]));
+        }
+    }
+}
+
 // Coordinate descent over the selected sub-blocks for rows [r0, r0 + rs) (src/engine.rs:600-658).
 template <int BM, bool SPLIT = false>
 __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, const TileSmem& sm, double& my_delta,
@@ -461,6 +483,9 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                     const float hjj = hss_full ? hss[jj * wd + jj] : hss[jj];
                     const float cur = wqs[jj * LDW + r];
                     const float gj = gt[jj * LD + r];
+                    // most steps keep their code: prove it without the two divisions (identical inputs in the
+                    // row's P threads, so they skip together; nothing shared changes, so no warp sync)
+                    if (cd_keeps_code(gj, hjj, cur, sc, __fsub_rn((float)cs[jj * CSLD + r], z))) continue;
                     const float target = __fadd_rn(cur, __fdiv_rn(gj, hjj));
                     float q = __fadd_rn(roundf(__fdiv_rn(target, sc)), z);
                     if (q < 0.0f) q = 0.0f;
@@ -475,19 +500,11 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
                             const float t2 = __fmul_rn(__fmul_rn(de, de), hjj);
                             row_delta = __dadd_rn(row_delta, (double)__fadd_rn(t1, t2));
                         }
-                        if (hss_full) {
-                            const float* hrow = hss + jj * wd;
-                            for (int kk = h; kk < wd; kk += P) {
-                                float* gp = &gt[kk * LD + r];
-                                *gp = __fadd_rn(*gp, __fmul_rn(de, hrow[kk]));
-                            }
-                        } else {
-                            const float* hrow = H + (int64_t)j * n + c0;
-                            for (int kk = h; kk < wd; kk += P) {
-                                float* gp = &gt[kk * LD + r];
-                                *gp = __fadd_rn(*gp, __fmul_rn(de, __ldg(hrow + kk)));
-                            }
-                        }
+                        if (hss_full)
+                            rank1_update<P, LD>(gt, r, h, wd, de, [&](int kk) { return hss[jj * wd + kk]; });
+                        else
+                            rank1_update<P, LD>(gt, r, h, wd, de,
+                                                [&](int kk) { return __ldg(H + (int64_t)j * n + c0 + kk); });
                         // every thread of the row has read column jj's code and W_hat before they change
                         __syncwarp(pmask);
                         if (h == 0) {
