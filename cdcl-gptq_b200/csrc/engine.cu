@@ -367,8 +367,7 @@ static int factor_launch(FactorGroup& g, const cdclq_config& cfg) {
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(items_dev, items.data(), sizeof(PrepItem) * nb, cudaMemcpyHostToDevice, g.st));
     if ((rc = launch_prepare(items_dev, (int)nb, (int)n, cfg.damp, g.st))) return rc;
     if (!g.h32_only) {
-        if ((rc = launch_cholesky(items_dev, (int)nb, (int)n, g.st))) return rc;
-        if ((rc = launch_tri_inverse(items_dev, (int)nb, (int)n, g.st))) return rc;
+        if ((rc = launch_factor(items_dev, (int)nb, (int)n, g.st))) return rc;
         if ((rc = launch_u_scatter(items_dev, (int)nb, (int)n, g.st))) return rc;
     }
     g.status.assign(nb, FactorStatus{0, -1, 0.0});

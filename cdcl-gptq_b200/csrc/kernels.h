@@ -28,8 +28,8 @@ struct PrepItem {
 };
 
 int launch_prepare(const PrepItem* items_dev, int nitems, int n, double damp, cudaStream_t st);
-int launch_cholesky(const PrepItem* items_dev, int nitems, int n, cudaStream_t st);
-int launch_tri_inverse(const PrepItem* items_dev, int nitems, int n, cudaStream_t st);
+// damped f64 Cholesky then triangular inverse of every item (src/linalg.rs:200-347), pipelined over two streams
+int launch_factor(const PrepItem* items_dev, int nitems, int n, cudaStream_t st);
 int launch_u_scatter(const PrepItem* items_dev, int nitems, int n, cudaStream_t st);
 
 // Stand-alone linalg entry points (single matrix, device pointers); used by the C ABI wrappers.

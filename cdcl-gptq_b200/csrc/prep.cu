@@ -18,6 +18,7 @@
 // FP64 runs on the SIMT DFMA pipe: on B200 its peak equals the FP64 tensor-core (DMMA) peak, and DMMA would
 // not reproduce the fixed summation order.
 #include <cmath>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -621,18 +622,67 @@ static void free_tables(ArgTables& t, cudaStream_t st) {
     t.tri = nullptr;
 }
 
-int launch_cholesky(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
+// Cholesky and triangular inverse of a batch, pipelined over two streams.  Step s of the inverse reads only
+// the block row s of L (columns < s + 96), which is final once the Cholesky's diagonal kernel of step s has run:
+// later panel solves and trailing updates write rows >= s + 96 only.  So the inverse runs on a second stream,
+// each step waiting for an event recorded after that diagonal kernel, and its latency-bound steps (diagonal
+// inverses, the early narrow products) overlap the Cholesky's trailing updates.  Same kernels, same operands,
+// same results as running the two one after the other.
+int launch_factor(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
     ArgTables t;
     int rc = make_tables(items_dev, nitems, st, t);
-    if (!rc) rc = run_cholesky(t.chol, nitems, n, st);
-    free_tables(t, st);
-    return rc;
-}
-
-int launch_tri_inverse(const PrepItem* items_dev, int nitems, int n, cudaStream_t st) {
-    ArgTables t;
-    int rc = make_tables(items_dev, nitems, st, t);
-    if (!rc) rc = run_tri_inverse(t.tri, nitems, n, st);
+    if (rc) return rc;
+    const int steps = (n + NB - 1) / NB;
+    std::vector<cudaEvent_t> ev(steps + 1, nullptr);
+    cudaStream_t st2 = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&st2, cudaStreamNonBlocking);
+    for (int i = 0; i <= steps && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev[steps], st);  // the argument tables and the prepared matrices
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st2, ev[steps], 0);
+    if (e != cudaSuccess) rc = cuda_error(e, "factorisation streams");
+    cudaFuncSetAttribute(chol_trail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DTile2<4>::SMEM_BYTES);
+    cudaFuncSetAttribute(chol_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CHOL_DIAG_SMEM);
+    const size_t smem_nb = (size_t)NB * NB * sizeof(double);
+    cudaFuncSetAttribute(chol_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_nb);
+    cudaFuncSetAttribute(tri_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_nb);
+    for (int i = 0; i < steps && !rc; i++) {
+        const int k = i * NB, kb = min(NB, n - k), kend = k + kb;
+        CDCLQ_LAUNCH(chol_diag_kernel, nitems, 256, CHOL_DIAG_SMEM, st, t.chol, n, k, kb);
+        e = cudaEventRecord(ev[i], st);
+        if (e != cudaSuccess) {
+            rc = cuda_error(e, "factorisation event");
+            break;
+        }
+        if (kend < n) {
+            const int rows_below = n - kend;
+            dim3 gp((rows_below + 127) / 128, nitems);
+            CDCLQ_LAUNCH(chol_panel_kernel, gp, 128, smem_nb, st, t.chol, n, k, kb);
+            dim3 gt((unsigned)chol_trail_tiles(rows_below), nitems);
+            CDCLQ_LAUNCH(chol_trail_kernel, gt, 256, DTile2<4>::SMEM_BYTES, st, t.chol, n, k, kb);
+        }
+        // inverse step i on the second stream, after block row i of L is final
+        e = cudaStreamWaitEvent(st2, ev[i], 0);
+        if (e != cudaSuccess) {
+            rc = cuda_error(e, "factorisation event wait");
+            break;
+        }
+        CDCLQ_LAUNCH(tri_diag_kernel, nitems, 128, smem_nb, st2, t.tri, n, k, kb);
+        if (k > 0) {
+            dim3 g((k + 63) / 64, nitems);
+            CDCLQ_LAUNCH(tri_gemm1_kernel, g, 256, DTile2<3>::SMEM_BYTES, st2, t.tri, n, k, kb);
+            CDCLQ_LAUNCH(tri_gemm2_kernel, g, 256, 0, st2, t.tri, n, k, kb);
+        }
+    }
+    if (!rc && (e = cudaGetLastError()) != cudaSuccess) rc = cuda_error(e, "factorisation kernels launch");
+    // join: the caller's stream continues after both chains (also on an error, so nothing is left in flight
+    // on the second stream when the tables are released)
+    if (st2 && ev[steps]) {
+        cudaEventRecord(ev[steps], st2);
+        cudaStreamWaitEvent(st, ev[steps], 0);
+    }
+    for (auto x : ev)
+        if (x) cudaEventDestroy(x);
+    if (st2) cudaStreamDestroy(st2);
     free_tables(t, st);
     return rc;
 }

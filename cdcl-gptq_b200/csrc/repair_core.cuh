@@ -175,18 +175,36 @@ __device__ void gemm_to_tile_cs(const AM& am, const float* b, int64_t ldb, int64
 
 // Tile staging between the row-major global matrices and the [col][row] shared-memory tiles.  A thread moves
 // one column of four consecutive rows: its global accesses are coalesced across the warp (consecutive
-// columns), and its shared-memory word lands in a distinct bank per column (strides CSLD / LDW).
+// columns), and its shared-memory word lands in a distinct bank per column (strides CSLD / LDW).  Each thread
+// takes STAGE_U such items at a time and issues all their global loads before its shared-memory stores, so
+// the loads of a pass are in flight together.
+constexpr int STAGE_U = 4;
+
 template <int BM>
 __device__ __forceinline__ void stage_codes(uint8_t* cs, const uint8_t* codes, int64_t n, int c0, int rs, int wd) {
     constexpr int CSLD = RepairTiles<BM>::CSLD;
-    const int quads = (rs + 3) >> 2;
-    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
-        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
-        uint32_t word = 0;
+    const int total = ((rs + 3) >> 2) * wd;
+    for (int base = threadIdx.x; base < total; base += STAGE_U * blockDim.x) {
+        uint32_t word[STAGE_U];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-            if (r + i < rs) word |= (uint32_t)codes[(int64_t)(r + i) * n + c0 + k] << (8 * i);
-        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+        for (int u = 0; u < STAGE_U; u++) {
+            const int idx = base + u * blockDim.x;
+            word[u] = 0;
+            if (idx < total) {
+                const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (r + i < rs) word[u] |= (uint32_t)codes[(int64_t)(r + i) * n + c0 + k] << (8 * i);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < STAGE_U; u++) {
+            const int idx = base + u * blockDim.x;
+            if (idx < total) {
+                const int q = idx / wd, k = idx - q * wd;
+                *reinterpret_cast<uint32_t*>(cs + k * CSLD + 4 * q) = word[u];
+            }
+        }
     }
 }
 
@@ -194,19 +212,39 @@ template <int BM>
 __device__ __forceinline__ void stage_cd_tiles(uint8_t* cs, float* wqs, const uint8_t* codes, const float* wq,
                                                int64_t n, int c0, int rs, int wd) {
     constexpr int CSLD = RepairTiles<BM>::CSLD, LDW = RepairTiles<BM>::LDW;
-    const int quads = (rs + 3) >> 2;
-    for (int idx = threadIdx.x; idx < quads * wd; idx += blockDim.x) {
-        const int q = idx / wd, k = idx - q * wd, r = 4 * q;
-        uint32_t word = 0;
+    const int total = ((rs + 3) >> 2) * wd;
+    for (int base = threadIdx.x; base < total; base += STAGE_U * blockDim.x) {
+        uint32_t word[STAGE_U];
+        float v[STAGE_U][4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            if (r + i < rs) {
-                const int64_t off = (int64_t)(r + i) * n + c0 + k;
-                word |= (uint32_t)codes[off] << (8 * i);
-                wqs[k * LDW + r + i] = wq[off];
+        for (int u = 0; u < STAGE_U; u++) {
+            const int idx = base + u * blockDim.x;
+            word[u] = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[u][i] = 0.0f;
+            if (idx < total) {
+                const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    if (r + i < rs) {
+                        const int64_t off = (int64_t)(r + i) * n + c0 + k;
+                        word[u] |= (uint32_t)codes[off] << (8 * i);
+                        v[u][i] = wq[off];
+                    }
+                }
             }
         }
-        *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word;
+#pragma unroll
+        for (int u = 0; u < STAGE_U; u++) {
+            const int idx = base + u * blockDim.x;
+            if (idx < total) {
+                const int q = idx / wd, k = idx - q * wd, r = 4 * q;
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (r + i < rs) wqs[k * LDW + r + i] = v[u][i];
+                *reinterpret_cast<uint32_t*>(cs + k * CSLD + r) = word[u];
+            }
+        }
     }
 }
 
@@ -378,14 +416,37 @@ __device__ void refit_tile(const ChunkInfo& ci, int r0, int rs, const TileSmem& 
             }
         }
         __syncthreads();
-        for (int idx = tid; idx < rs * wd && writer; idx += blockDim.x) {
-            int rr = idx / wd, k = idx - rr * wd;
-            if (sm.accept[rr]) {
-                float u = __fsub_rn((float)cs[k * CSLD + rr], sm.zrow[rr]);
-                float ndq = __fmul_rn(sm.snew[rr], u);
-                int64_t off = (int64_t)rr * n + c0 + k;
-                E[off] = __fadd_rn(E[off], __fsub_rn(WQ[off], ndq));
-                WQ[off] = ndq;
+        // accepted rows: W_hat = s_new * u and E += W_hat_old - W_hat_new over the group (loads batched)
+        const int total = writer ? rs * wd : 0;
+        for (int base = tid; base < total; base += STAGE_U * blockDim.x) {
+            float ev[STAGE_U], wv[STAGE_U];
+#pragma unroll
+            for (int u = 0; u < STAGE_U; u++) {
+                const int idx = base + u * blockDim.x;
+                ev[u] = 0.0f;
+                wv[u] = 0.0f;
+                if (idx < total) {
+                    const int rr = idx / wd, k = idx - rr * wd;
+                    if (sm.accept[rr]) {
+                        const int64_t off = (int64_t)rr * n + c0 + k;
+                        ev[u] = E[off];
+                        wv[u] = WQ[off];
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < STAGE_U; u++) {
+                const int idx = base + u * blockDim.x;
+                if (idx < total) {
+                    const int rr = idx / wd, k = idx - rr * wd;
+                    if (sm.accept[rr]) {
+                        const float uc = __fsub_rn((float)cs[k * CSLD + rr], sm.zrow[rr]);
+                        const float ndq = __fmul_rn(sm.snew[rr], uc);
+                        const int64_t off = (int64_t)rr * n + c0 + k;
+                        E[off] = __fadd_rn(ev[u], __fsub_rn(wv[u], ndq));
+                        WQ[off] = ndq;
+                    }
+                }
             }
         }
         __syncthreads();
@@ -450,9 +511,16 @@ __device__ void cd_tile(const ChunkInfo& ci, int r0, int rs, int cd_sweeps, cons
         if (SPLIT) cluster_sync_all();  // the partner's codes / W_hat / E / scale writes are visible
         stage_cd_tiles<BM>(cs, wqs, CODES, WQ, n, c0, rs, wd);
         if (hss_full) {
-            for (int idx = tid; idx < wd * wd; idx += blockDim.x) {
-                int a = idx / wd, b = idx - a * wd;
-                hss[idx] = __ldg(H + (int64_t)(c0 + a) * n + c0 + b);
+            for (int base = tid; base < wd * wd; base += STAGE_U * blockDim.x) {
+                float hv[STAGE_U];
+#pragma unroll
+                for (int u = 0; u < STAGE_U; u++) {
+                    const int idx = base + u * blockDim.x, a = idx / wd, b = idx - a * wd;
+                    hv[u] = idx < wd * wd ? __ldg(H + (int64_t)(c0 + a) * n + c0 + b) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < STAGE_U; u++)
+                    if (base + u * blockDim.x < wd * wd) hss[base + u * blockDim.x] = hv[u];
             }
         } else {
             for (int a = tid; a < wd; a += blockDim.x) hss[a] = __ldg(H + (int64_t)(c0 + a) * n + c0 + a);
