@@ -502,9 +502,10 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
                                              uo.data(), 1, st);
     }
     if ((rc = rt_agree(rt, rc))) return rc;
-    // The factors travel on the communication stream, ordered after this rank's factorisations; meanwhile the
-    // layers whose factor this rank computed itself (wave A) are quantized on the work stream, and the other
-    // layers (wave B) once every factor has landed.  With a skeleton the factors are per layer: one wave.
+    // The factors travel on the communication stream, ordered after this rank's factorisations; every layer is
+    // then quantized in one batch once they have landed.  (Quantizing the layers whose factor this rank computed
+    // first, in a batch of their own, would hide the broadcast - tens of milliseconds over NVLink - but give
+    // the repair two launches, each ending on its own tail of wide row chunks: measured slower at N = 2.)
     cudaEvent_t ev_f = nullptr, ev_b = nullptr;
     CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_f, cudaEventDisableTiming));
     CDCLQ_CUDA_TRY(cudaEventCreateWithFlags(&ev_b, cudaEventDisableTiming));
@@ -531,24 +532,23 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
     }
     CDCLQ_CUDA_TRY(cudaEventRecord(ev_b, rt->comm_st));
 
-    // ---- this rank's rows, one batch per wave and row chunk (layers whose automatic row chunk differs)
+    // ---- this rank's rows, one batch per row chunk (layers whose automatic row chunk differs)
     std::vector<cdclq_layer_stats> lst(nly);
     std::vector<std::vector<uint32_t>> scratch_perm(nly);
     std::vector<std::vector<uint8_t>> scratch_gb(nly);
-    std::map<std::pair<int, size_t>, std::vector<size_t>> by_rc;  // (wave, row chunk) -> layers
+    std::map<size_t, std::vector<size_t>> by_rc;  // row chunk -> layers
     for (size_t l = 0; l < nly; l++)
-        if (part[l].r1 > part[l].r0) by_rc[{(!skel && owner[ly[l].input] == me) ? 0 : 1, part[l].rc}].push_back(l);
+        if (part[l].r1 > part[l].r0) by_rc[part[l].rc].push_back(l);
     std::vector<cdclq_batch_input> in_dev(nin);
     for (size_t i = 0; i < nin; i++) in_dev[i] = cdclq_batch_input{hdev[i], ns[i]};
-    bool waited = false;
+    {
+        cudaError_t e = cudaStreamWaitEvent(st, ev_b, 0);
+        if (e != cudaSuccess) return cuda_error(e, "factor broadcast wait");
+    }
     for (auto& kv : by_rc) {
         if (rc) break;
-        if (kv.first.first == 1 && !waited) {
-            CDCLQ_CUDA_TRY(cudaStreamWaitEvent(st, ev_b, 0));
-            waited = true;
-        }
         cdclq_config c = cfg;
-        c.row_chunk = kv.first.second;
+        c.row_chunk = kv.first;
         std::vector<cdclq_batch_layer> d(kv.second.size());
         for (size_t k = 0; k < kv.second.size(); k++) {
             const size_t l = kv.second[k];
@@ -572,10 +572,6 @@ int runtime_quantize_batch(Runtime* rt, const cdclq_batch_input* in, size_t nin,
         }
         rc = skel ? cdclq_quantize_batch(in_dev.data(), nin, d.data(), d.size(), &c, 1, st)
                   : cdclq_quantize_batch_prepared(in_dev.data(), nin, u.data(), d.data(), d.size(), &c, 1, st);
-    }
-    if (!waited) {  // no wave B rows here: the factors still land before this call returns
-        cudaError_t e = cudaStreamWaitEvent(st, ev_b, 0);
-        if (!rc && e != cudaSuccess) rc = cuda_error(e, "factor broadcast wait");
     }
     if ((rc = rt_agree(rt, rc))) return rc;
 
