@@ -721,6 +721,7 @@ def north_star(torch, rank, world, rt, bits=4, group=64):
     names = ("hessians", "hessian_broadcast", "quantization")
     clock = PhaseClock(torch, st, names)
     eng = {k: 0.0 for k in ("ms_prepare", "ms_phase1", "ms_stats", "ms_repair", "ms_final")}
+    factor_batches, free_gb = 0, []
     stats = []
     with torch.cuda.stream(st):
         owner = assign_owners([n for (_, n) in inputs], world, 2)
@@ -755,12 +756,14 @@ def north_star(torch, rank, world, rt, bits=4, group=64):
                  for j, (_, d_out, n, _) in enumerate(part)]
             b = RuntimeBatch(torch, rt, part_l, part_in, [H[i] for i in used], W, cfg, on_device=True)
             torch.cuda.synchronize()
+            free_gb.append(round(torch.cuda.mem_get_info()[0] / 2 ** 30, 1))
             if world > 1:
                 torch.distributed.barrier()
             clock(lambda: b.run(gather=False), "quantization")
             prof = __import__("cdclq")._lib.last_run_profile()
             for k in eng:
                 eng[k] += prof[k]
+            factor_batches += int(prof.get("factor_batches", 0))
             stats.extend(b.stats)
             del W, b
             torch.cuda.empty_cache()
@@ -775,6 +778,7 @@ def north_star(torch, rank, world, rt, bits=4, group=64):
         "refine_frac": cfg.refine_frac, "row_chunk": ROW_CHUNK,
         "phases_s_max_over_ranks": {k: v * 1e-3 for k, v in zip(names, t[1:])},
         "engine_phases_ms_rank0": eng,
+        "factor_batches_rank0": factor_batches, "free_gib_before_each_batch_rank0": free_gb,
         "loss_gptq": sum(s.loss_gptq for s in stats), "loss_final": sum(s.loss_final for s in stats),
         "timed": "tensor-core Hessian accumulation + Hessian broadcast + quantization through the runtime "
                  "(synthetic activation and weight generation excluded)",

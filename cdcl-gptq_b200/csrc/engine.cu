@@ -324,11 +324,16 @@ static size_t factor_item_bytes(size_t n, bool h32_only = false) {
     return 2 * n * n * sizeof(double) + 96 * n * sizeof(double) + n * sizeof(double) + 256;
 }
 
+// Streams of the factorisation groups.  Stream 0 carries the widest group (groups are ordered widest first),
+// whose chain of block steps is the longest, so it gets the device's highest stream priority: its latency-bound
+// diagonal and panel kernels then take SMs ahead of the narrower groups' launches.
 static cudaStream_t pool_stream(size_t i) {
     static thread_local std::vector<cudaStream_t> pool;
     while (pool.size() <= i) {
         cudaStream_t s = nullptr;
-        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+        int least = 0, greatest = 0;
+        cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, pool.empty() ? greatest : least);
         pool.push_back(s);
     }
     return pool[i];
@@ -472,16 +477,40 @@ static int factorize_groups(std::vector<FactorGroup>& groups, const cdclq_config
         }
         return rc;
     }
-    for (auto& g : groups) {
-        size_t max_items = std::max<size_t>(1, budget / factor_item_bytes(g.n, g.h32_only));
-        for (g.b0 = 0; g.b0 < g.hs.size(); g.b0 += max_items) {
-            g.nb = std::min(max_items, g.hs.size() - g.b0);
+    // Not everything fits at once: each width group gets a share of the budget in proportion to its need and
+    // works through its inputs in sub-batches of that size on its own stream; one sub-batch of every unfinished
+    // group is in flight at a time, so the groups still overlap.
+    std::vector<size_t> max_items(groups.size());
+    for (size_t k = 0; k < groups.size(); k++) {
+        const size_t item = factor_item_bytes(groups[k].n, groups[k].h32_only);
+        const double share = (double)budget * (double)(item * groups[k].hs.size()) / (double)need;
+        max_items[k] = std::max<size_t>(1, (size_t)(share / (double)item));
+        groups[k].b0 = 0;
+    }
+    for (bool more = true; more && !rc;) {
+        more = false;
+        std::vector<size_t> live;
+        for (size_t k = 0; k < groups.size() && !rc; k++) {
+            FactorGroup& g = groups[k];
+            if (g.b0 >= g.hs.size()) continue;
+            g.nb = std::min(max_items[k], g.hs.size() - g.b0);
             if (batches) *batches += 1;
-            if ((rc = factor_launch(g, cfg))) return rc;
-            if ((rc = factor_finish(g))) return rc;
+            if ((rc = factor_launch(g, cfg))) {  // nothing to read back: wait for what was issued, release it
+                cudaStreamSynchronize(g.st);
+                g.ar.reset();
+                break;
+            }
+            live.push_back(k);
+        }
+        for (size_t k : live) {
+            FactorGroup& g = groups[k];
+            const int r2 = factor_finish(g);
+            if (!rc) rc = r2;
+            g.b0 += g.nb;
+            if (g.b0 < g.hs.size()) more = true;
         }
     }
-    return 0;
+    return rc;
 }
 
 // The whole path for a batch of layers.  `cache` (single-layer calls only) is the one-entry memo.
@@ -1433,10 +1462,10 @@ int cdclq_prepare_factors(const cdclq_batch_input* inputs, size_t n_inputs, cons
         by_n[n].push_back(k);
     }
     std::vector<FactorGroup> groups;
-    for (auto& kv : by_n) {
+    for (auto it = by_n.rbegin(); it != by_n.rend(); ++it) {  // widest first: the longest factorisations
         FactorGroup g;
-        g.n = kv.first;
-        for (size_t k : kv.second) {
+        g.n = it->first;
+        for (size_t k : it->second) {
             g.hs.push_back(h_dev[k]);
             g.es.push_back(&preps[k]);
         }

@@ -635,7 +635,9 @@ int launch_factor(const PrepItem* items_dev, int nitems, int n, cudaStream_t st)
     const int steps = (n + NB - 1) / NB;
     std::vector<cudaEvent_t> ev(steps + 1, nullptr);
     cudaStream_t st2 = nullptr;
-    cudaError_t e = cudaStreamCreateWithFlags(&st2, cudaStreamNonBlocking);
+    int prio = 0;
+    cudaStreamGetPriority(st, &prio);  // the inverse runs at its Cholesky's priority
+    cudaError_t e = cudaStreamCreateWithPriority(&st2, cudaStreamNonBlocking, prio);
     for (int i = 0; i <= steps && e == cudaSuccess; i++) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventRecord(ev[steps], st);  // the argument tables and the prepared matrices
     if (e == cudaSuccess) e = cudaStreamWaitEvent(st2, ev[steps], 0);

@@ -171,3 +171,27 @@ def test_factorisation_sub_batches(gpu, monkeypatch):
         assert np.array_equal(o["codes"], qb.codes) and np.array_equal(o["scales"], qb.scales)
         assert np.array_equal(o["zeros"], qb.zeros) and np.array_equal(o["perm"], qb.perm)
         assert stats[i].loss_gptq == sb.loss_gptq
+
+
+def test_factorisation_sub_batches_two_widths(gpu, monkeypatch):
+    """Two width groups under a factorisation budget smaller than their need: each group works through its inputs
+    in sub-batches of its share of the budget on its own stream, one sub-batch of each group in flight at a time;
+    the results are the oracle's."""
+    import cdclq
+
+    widths = (2048, 2048, 1024, 1024)
+    hs = [np.ascontiguousarray(orc.problem(1, n, 2600, 700 + i)[1]) for i, n in enumerate(widths)]
+    ws = [orc.rng_normal(710 + i, 128 * n, 0.02).reshape(128, n) for i, n in enumerate(widths)]
+    cfg = wc._cfg(bits=3, group=128, mse_grid=True)
+    item = 2 * 8 * 2048 * 2048 + 97 * 8 * 2048 + 256  # the engine's per-item estimate at n = 2048
+    monkeypatch.setenv("CDCLQ_FACTOR_BUDGET_BYTES", str(int(1.5 * item)))  # one input of each width at a time
+    outs, stats = _batch(hs, [(i, ws[i]) for i in range(len(widths))], cfg)
+    prof = cdclq._lib.last_run_profile()
+    assert prof["factor_batches"] >= 4, prof["factor_batches"]
+    for i, n in enumerate(widths):
+        qb, sb = orc.quantize_layer(ws[i], 128, n, hs[i], None, "x", cfg)
+        o = outs[i]
+        assert np.array_equal(o["codes"], qb.codes) and np.array_equal(o["scales"], qb.scales)
+        assert np.array_equal(o["zeros"], qb.zeros) and np.array_equal(o["perm"], qb.perm)
+        assert stats[i].loss_gptq == sb.loss_gptq
+        assert abs(stats[i].loss_final - sb.loss_final) <= 1e-9 * sb.loss_final
