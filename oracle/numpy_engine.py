@@ -28,6 +28,15 @@ import numpy as np
 F16_MIN_NORMAL = np.float32(6.1035156e-5)
 F32 = np.float32
 
+# The product used for the repair's block gradients (G = E H[:, cols], u H_CC).  None: numpy's BLAS in f32.  A
+# caller may set another f32 product here to study how a different arithmetic for those GEMMs (a tensor-core
+# emulation, say) changes the repair's decisions; tests/test_numpy_restatement.py does.
+REPAIR_MATMUL = None
+
+
+def _repair_mm(a, b):
+    return (REPAIR_MATMUL(a, b) if REPAIR_MATMUL is not None else a @ b).astype(np.float32)
+
 
 def round_f16(x):
     """src/quant.rs:24-26: nearest f16 (ties to even), widened back to f32."""
@@ -192,10 +201,10 @@ def process_chunk(wt, u, h, gbits, g, cfg):
             changed = 0
             for gi in range(ng):
                 c0, c1 = gi * g, min(gi * g + g, n)
-                gs = (e @ h[:, c0:c1]).astype(np.float32)
+                gs = _repair_mm(e, h[:, c0:c1])
                 hcc = h[c0:c1, c0:c1]
                 uu = (codes[:, c0:c1] - zeros[:, gi][:, None]).astype(np.float32)
-                hu = (uu @ hcc).astype(np.float32)
+                hu = _repair_mm(uu, hcc)
                 num = np.zeros(rows, np.float32)
                 den = np.zeros(rows, np.float32)
                 for k in range(c1 - c0):  # sequential f32 sums, as the reference's iterator sums
@@ -230,7 +239,7 @@ def process_chunk(wt, u, h, gbits, g, cfg):
                 for s in sel:
                     c0, c1 = s * sbw, min((s + 1) * sbw, n)
                     wd = c1 - c0
-                    gs = (e @ h[:, c0:c1]).astype(np.float32)
+                    gs = _repair_mm(e, h[:, c0:c1])
                     hss = h[c0:c1, c0:c1]
                     active = np.ones(rows, bool)
                     deltas = np.zeros(rows)  # per-row running sums, added in row order below

@@ -80,3 +80,59 @@ def test_numpy_find_params_matches_oracle():
             s1, z1 = orc.find_params(vals, bits, mse)
             s2, z2 = ne.find_params(vals, bits, mse)
             assert np.array_equal(s1, s2) and np.array_equal(z1, z2), (bits, mse)
+
+
+# ---- What a tensor-core repair would do to parity ---------------------------------------------------------
+# The repair's block gradients (G = E H[:, cols], u H_CC) run on the FP32 pipe in the oracle's fixed order.  A
+# tcgen05 replacement would compute them from TF32 operands with f32 accumulation.  The numpy restatement can
+# take another product for those GEMMs (numpy_engine.REPAIR_MATMUL); these emulate the tensor core: operands
+# rounded to TF32 (10-bit mantissa, round to nearest even), products of a K block of 8 summed exactly and rounded
+# to f32, the blocks accumulated in one f32 accumulator in K order.  "3xTF32" splits each operand into a TF32
+# head and a TF32 tail and sums head*head + head*tail + tail*head; "1xTF32" uses the heads alone.
+
+def _tf32(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0xFFF + ((u >> 13) & 1)) & ~np.uint64(0x1FFF)
+    return u.astype(np.uint32).view(np.float32)
+
+
+def _kblock_f32(parts, kb=8):
+    a0, b0 = parts[0]
+    acc = np.zeros((a0.shape[0], b0.shape[1]), np.float32)
+    for k0 in range(0, a0.shape[1], kb):
+        blk = np.zeros(acc.shape, np.float64)
+        for a, b in parts:
+            blk += a[:, k0:k0 + kb].astype(np.float64) @ b[k0:k0 + kb].astype(np.float64)
+        acc = (acc + blk.astype(np.float32)).astype(np.float32)
+    return acc
+
+
+def _mm_3xtf32(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    ah, bh = _tf32(a), _tf32(b)
+    return _kblock_f32([(ah, bh), (ah, _tf32(b - bh)), (_tf32(a - ah), bh)])
+
+
+def _mm_1xtf32(a, b):
+    return _kblock_f32([(_tf32(np.asarray(a, np.float32)), _tf32(np.asarray(b, np.float32)))])
+
+
+def test_tensor_core_repair_emulation(monkeypatch):
+    """3xTF32 block gradients keep the repair's decisions (the north star's bar holds: here every code and scale is
+    identical), TF32 alone does not (scales accepted differently).  Measured the same way on a configs[1]-shaped
+    slice (256 rows x 2048 columns, 3-bit g128 --mse-grid, 10 passes): 3xTF32 100 % identical codes and scales,
+    1xTF32 99.75 % codes and 68 % scales."""
+    d_out, n = 128, 512
+    cfg = Config(bits=3, group=128, block=128, sub_block=64, mse_grid=True, passes=10, tol=1e-3, row_chunk=128)
+    w, h = orc.problem(d_out, n, 2 * n, 21)
+    qb, sb = orc.quantize_layer(w, d_out, n, h, None, "x", cfg)
+    perm, _ = orc.compute_perm(h, w, d_out, n, cfg)
+    u, h32, _ = orc.build_prepared(h, n, perm, cfg)
+    monkeypatch.setattr(ne, "REPAIR_MATMUL", _mm_3xtf32)
+    a3 = agreement(ne.quantize_layer(w, h, cfg, prepared=(perm, u, h32)), qb, sb)
+    monkeypatch.setattr(ne, "REPAIR_MATMUL", _mm_1xtf32)
+    a1 = agreement(ne.quantize_layer(w, h, cfg, prepared=(perm, u, h32)), qb, sb)
+    print("3xTF32", a3, "1xTF32", a1)
+    assert a3["codes"] >= 0.9999 and a3["scales"] >= 0.9999 and a3["loss_final"] <= 1e-6
+    assert a1["scales"] < 0.9999  # TF32 alone misses the bar
