@@ -54,6 +54,12 @@ CASES = [
     ("defaults_rows300", 300, 256, 1200, 21, Config(row_chunk=128)),
     ("mse_grid", 96, 256, 1000, 22, Config(mse_grid=True, row_chunk=32, passes=4)),
     ("g_gt_b", 40, 256, 900, 23, Config(group=64, block=32, sub_block=32, row_chunk=16)),
+    # group starts, U-window ends and block ends that cut the GPTQ pass's 8-column micro-blocks short
+    ("group_20_block_40", 40, 200, 900, 46, Config(group=20, block=40, sub_block=10, row_chunk=16)),
+    ("group_12_block_36_mse", 40, 216, 900, 47, Config(bits=4, group=12, block=36, sub_block=12, mse_grid=True,
+                                                       row_chunk=16)),
+    ("group_13_block_26_actorder", 36, 130, 700, 48, Config(bits=3, group=13, block=26, sub_block=7, act_order=True,
+                                                            row_chunk=12)),
     ("g_eq_n", 40, 192, 900, 24, Config(group=0, block=64, sub_block=48, row_chunk=40)),
     ("b_gt_g_4bit", 72, 256, 900, 25, Config(bits=4, group=16, block=128, sub_block=32, row_chunk=24)),
     ("2bit_g64_mse", 64, 256, 900, 26, Config(bits=2, group=64, block=64, mse_grid=True, refine_frac=0.25,
