@@ -317,6 +317,7 @@ struct FactorGroup {
     double* damp_dev = nullptr;
     std::vector<FactorStatus> status;
     std::vector<double> damp;
+    bool launched = false;          // a sub-batch is in flight: factor_finish reads its status back
 };
 
 static size_t factor_item_bytes(size_t n, bool h32_only = false) {
@@ -379,12 +380,17 @@ static int factor_launch(FactorGroup& g, const cdclq_config& cfg) {
     g.damp.assign(nb, 0.0);
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(g.status.data(), g.status_dev, sizeof(FactorStatus) * nb, cudaMemcpyDeviceToHost, g.st));
     CDCLQ_CUDA_TRY(cudaMemcpyAsync(g.damp.data(), g.damp_dev, sizeof(double) * nb, cudaMemcpyDeviceToHost, g.st));
+    g.launched = true;
     return 0;
 }
 
+// Waits for the group's sub-batch, releases its work memory and reads its status back (nothing to read when its
+// launch failed part-way, or never happened because an earlier group's failed).
 static int factor_finish(FactorGroup& g) {
     CDCLQ_CUDA_TRY(cudaStreamSynchronize(g.st));
     g.ar.reset();
+    if (!g.launched) return 0;
+    g.launched = false;
     for (size_t i = 0; i < g.nb; i++) {
         if (g.status[i].err) {
             return set_error(CDCLQ_ERR_NOT_PD, "matrix is not positive definite (pivot " +
